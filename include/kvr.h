@@ -1,0 +1,219 @@
+/*
+ * kvr.h -- C ABI of the B200-native packed draft-KV hot path.
+ *
+ * Every entry point takes plain device pointers, element counts and strides,
+ * enqueues its work on the given CUDA stream (a cudaStream_t passed as void*,
+ * NULL = legacy default stream) and returns an int status (KVR_OK = 0).  No
+ * entry point allocates device memory; callers pass outputs and workspaces.
+ *
+ * Tensor layouts follow kv_reduce/packed_kv_cache.py of the reference:
+ *   key payload    uint8  [B, H, P, D*kb/8]   codes LSB-first within bytes
+ *   key scale/off  bf16   [B, H, P/G, D]      (reference shape [B,H,P/G,1,D])
+ *   key residual   bf16   [B, H, S-P, D]      the BF16 window after the prefix
+ *   value payload  uint8  [B, H, S, D*vb/8]
+ *   value scale/off bf16  [B, H, S]           (reference shape [B,H,S,1])
+ * where P = floor(max(0, S-R)/G)*G  (packed_kv_cache.py:15-19).
+ * Each (b,h) slab is addressed through an explicit "bh stride", so the
+ * reference's contiguous slabs (stride = P*D*kb/8 ...) and a preallocated
+ * capacity layout (stride = capacity*...) are both accepted.
+ */
+#ifndef KVR_H_
+#define KVR_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* kvr_stream_t;
+
+enum kvr_status {
+  KVR_OK = 0,
+  KVR_ERR_INVALID_ARGUMENT = 1,   /* bad size, bit width, null pointer ... */
+  KVR_ERR_UNSUPPORTED = 2,        /* valid for the reference, not built here */
+  KVR_ERR_MISALIGNED = 3,         /* pointer/stride breaks a 16-byte rule */
+  KVR_ERR_CUDA = 4,               /* a CUDA runtime call failed */
+  KVR_ERR_CAPACITY = 5,           /* streaming cache would overflow */
+  KVR_ERR_WORKSPACE = 6           /* workspace smaller than kvr_decode_plan asked */
+};
+
+#define KVR_MAX_LAYERS 32
+
+/* Library version (major*10000 + minor*100 + patch). */
+int kvr_version(void);
+/* Human-readable text for a kvr_status value. */
+const char* kvr_status_string(int status);
+/* Last CUDA error text seen by the library on this host thread ("" if none). */
+const char* kvr_last_error(void);
+
+/* ---------------------------------------------------------------- packing
+ * Replaces pack_unsigned (packed_kv_cache.py:28-63): n codes (uint8, each
+ * < 2^bits) -> ceil(n*bits/8) bytes, value i at bit i*bits, LSB first.
+ * bits in [1, 8].  Codes >= 2^bits are masked (the reference raises on the
+ * host; the Python layer keeps that check).                                */
+int kvr_pack_unsigned(const uint8_t* codes, int64_t n, int bits,
+                      uint8_t* payload, kvr_stream_t stream);
+
+/* Replaces unpack_unsigned (packed_kv_cache.py:66-94). */
+int kvr_unpack_unsigned(const uint8_t* payload, int64_t n, int bits,
+                        uint8_t* codes, kvr_stream_t stream);
+
+/* ------------------------------------------------------- quantize + pack
+ * Values, per-token affine: replaces pack_per_token_affine
+ * (packed_kv_cache.py:159-192).  x: bf16 rows of D elements; row r of
+ * (b,h) slab at x + bh*x_bh_stride + r*x_row_stride (elements).
+ * Writes rows [row0, row0+rows) of payload/scale/offset for every (b,h):
+ *   payload + bh*payload_bh_stride + (row0+r)*D*bits/8  (bytes)
+ *   scale/offset + bh*meta_bh_stride + row0 + r        (elements)
+ * bits in [2, 8].  When D*bits % 8 != 0 the reference's flat bitstream
+ * crosses rows: then the payload is that flat stream of [bh, rows, D]
+ * codes (payload_bh_stride unused), row0 must be 0 and `codes_scratch`
+ * (bh*rows*D bytes) carries the codes between the two passes.             */
+typedef struct {
+  const uint16_t* x; int64_t x_bh_stride; int64_t x_row_stride;
+  uint8_t* payload; int64_t payload_bh_stride;
+  uint16_t* scale; uint16_t* offset; int64_t meta_bh_stride;
+  int bh;          /* number of (b,h) slabs = B*H */
+  int rows;        /* tokens to quantize per slab */
+  int row0;        /* first destination token row */
+  int head_dim;    /* D */
+  int bits;
+  uint8_t* codes_scratch;   /* only for the generic path, else NULL */
+} kvr_token_quant_args;
+int kvr_quantize_per_token(const kvr_token_quant_args* a, kvr_stream_t stream);
+
+/* Keys, per-channel grouped affine over the token axis: replaces
+ * pack_per_channel_grouped_affine (packed_kv_cache.py:195-253) for the
+ * groups [group0, group0+groups) of every (b,h) slab.  Token t of a group
+ * g is x row (g-group0)*G + t.  Payload row index = g*G + t.
+ * scale/offset index = g*D + d (plus bh*meta_bh_stride).                  */
+typedef struct {
+  const uint16_t* x; int64_t x_bh_stride; int64_t x_row_stride;
+  uint8_t* payload; int64_t payload_bh_stride;
+  uint16_t* scale; uint16_t* offset; int64_t meta_bh_stride;
+  int bh;
+  int groups;      /* groups to quantize per slab */
+  int group0;      /* first destination group */
+  int group_size;  /* G */
+  int head_dim;
+  int bits;
+  uint8_t* codes_scratch;   /* D*bits % 8 != 0 only; group0 must be 0 */
+} kvr_group_quant_args;
+int kvr_quantize_grouped(const kvr_group_quant_args* a, kvr_stream_t stream);
+
+/* --------------------------------------------------------- dequantize
+ * Replaces PackedKVComponent.unpack() (packed_kv_cache.py:126-149):
+ * out = (code * scale + offset) in fp32 with separate roundings, then cast
+ * to out_dtype (0 = bf16, 1 = fp32, 2 = fp16).  For keys the BF16 residual rows
+ * [P, S) are copied after the dequantized prefix.                         */
+typedef struct {
+  const uint8_t* payload; int64_t payload_bh_stride;
+  const uint16_t* scale; const uint16_t* offset; int64_t meta_bh_stride;
+  const uint16_t* residual; int64_t residual_bh_stride;  /* keys only */
+  void* out;       /* [bh, seq_len, D] contiguous */
+  int out_dtype;   /* 0 bf16, 1 fp32, 2 fp16 */
+  int bh;
+  int seq_len;     /* S */
+  int prefix_len;  /* P (keys) ; ignored for values */
+  int group_size;  /* G (keys) ; 0 selects the per-token (value) layout */
+  int head_dim;
+  int bits;
+} kvr_dequant_args;
+int kvr_dequantize(const kvr_dequant_args* a, kvr_stream_t stream);
+
+/* ------------------------------------------------------- streaming cache
+ * One decode/draft step of PackedLayer.append (packed_review.py:23-31) on a
+ * preallocated capacity layout: n new tokens per (b,h).  Keys go to the
+ * BF16 residual rows [res_len, res_len+n); values are quantized per token
+ * into rows [seq_len, seq_len+n) of the value payload/scale/offset.
+ * Layout of the new tokens: k/v [bh, n, D] contiguous bf16.                */
+typedef struct {
+  const uint16_t* k; const uint16_t* v;
+  uint16_t* key_residual; int64_t key_residual_bh_stride;
+  uint8_t* value_payload; int64_t value_payload_bh_stride;
+  uint16_t* value_scale; uint16_t* value_offset; int64_t value_meta_bh_stride;
+  int bh, n, seq_len, res_len, res_capacity, seq_capacity, head_dim, value_bits;
+} kvr_append_args;
+int kvr_append(const kvr_append_args* a, kvr_stream_t stream);
+
+/* PackedLayer.commit (packed_review.py:32-41): quantize the first
+ * `groups` groups of the residual window into key groups
+ * [prefix_len/G, prefix_len/G + groups) and move the remaining
+ * res_len - groups*G residual rows to the front of `residual_out`
+ * (a second buffer; the caller swaps buffers after the call).             */
+typedef struct {
+  const uint16_t* residual_in; uint16_t* residual_out; int64_t residual_bh_stride;
+  uint8_t* key_payload; int64_t key_payload_bh_stride;
+  uint16_t* key_scale; uint16_t* key_offset; int64_t key_meta_bh_stride;
+  int bh, res_len, groups, prefix_len, prefix_capacity, group_size, head_dim, key_bits;
+} kvr_flush_args;
+int kvr_flush_groups(const kvr_flush_args* a, kvr_stream_t stream);
+
+/* -------------------------------------------------------- decode attention
+ * Replaces packed_kv_decode_attention (triton_packed_kv_attention.py:284-389)
+ * and its three kernels (:27-131, :134-248, :251-281): one-token GQA decode
+ * over the packed cache, split-K over tokens, online softmax in fp32, LSE
+ * merge of the splits fused into the same launch.  Several layers of equal
+ * geometry may share one launch (n_layers <= KVR_MAX_LAYERS).
+ * query/out: [B, HQ, 1, D] bf16 contiguous per layer.
+ * Supported: D in {64,128}; key/value bits in {2,4,8} (D=64 needs value
+ * bits >= 4); G a multiple of 16 with G <= 128 or G == 16*k; HQ/HKV <= 8.
+ * The caller passes a workspace of kvr_decode_plan() bytes for the split
+ * partials (scratch, any contents) and `counters`, kvr_decode_plan() ints
+ * that must be zero before the first launch; every completed launch leaves
+ * them zero again, so one counter array can serve a stream's launches.     */
+typedef struct {
+  const uint8_t* key_payload;
+  const uint16_t* key_scale;
+  const uint16_t* key_offset;
+  const uint16_t* key_residual;
+  const uint8_t* value_payload;
+  const uint16_t* value_scale;
+  const uint16_t* value_offset;
+  const uint16_t* query;
+  uint16_t* out;
+} kvr_layer_ptrs;
+
+typedef struct {
+  const kvr_layer_ptrs* layers;   /* host array of n_layers entries */
+  int n_layers;
+  int batch, q_heads, kv_heads, head_dim;
+  int seq_len, prefix_len, group_size, key_bits, value_bits;
+  int64_t key_payload_bh_stride;   /* bytes    */
+  int64_t key_meta_bh_stride;      /* elements */
+  int64_t key_residual_bh_stride;  /* elements */
+  int64_t value_payload_bh_stride; /* bytes    */
+  int64_t value_meta_bh_stride;    /* elements */
+  int split_tokens;   /* > 0: tokens per split (rounded up to 32); 0: auto */
+  int num_sms;        /* 0: query the current device */
+  void* workspace; size_t workspace_bytes;   /* split partials */
+  int* counters;      /* n_layers*batch*kv_heads ints, zero on entry */
+} kvr_decode_args;
+
+/* Fills the split count, workspace bytes and counter count for `a`
+ * (workspace and counters ignored). */
+int kvr_decode_plan(const kvr_decode_args* a, int* num_splits,
+                    size_t* workspace_bytes, size_t* counter_count);
+int kvr_decode_attention(const kvr_decode_args* a, kvr_stream_t stream);
+
+/* LSE merge of externally produced partials (the cross-GPU token split):
+ * parts: n_parts blocks of [rows] (m, l) pairs and [rows, D] unnormalised
+ * outputs, m in log2 units; out[rows, D] bf16 = sum_p 2^(m_p-M) o_p /
+ * sum_p 2^(m_p-M) l_p.  Rows with no mass are written as zero.            */
+int kvr_lse_merge(const float* part_ml, const float* part_o, int n_parts,
+                  int rows, int head_dim, uint16_t* out, kvr_stream_t stream);
+
+/* Partial decode for one shard of the token axis: same as
+ * kvr_decode_attention but over tokens [token_begin, token_end) only, with
+ * one split per (layer, b, kv head); writes (m, l) pairs to part_ml
+ * [n_layers*B*HQ] and unnormalised outputs to part_o [n_layers*B*HQ, D]
+ * instead of the final output (for kvr_lse_merge after an all-gather).     */
+int kvr_decode_partial(const kvr_decode_args* a, int token_begin, int token_end,
+                       float* part_ml, float* part_o, kvr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVR_H_ */

@@ -1,0 +1,205 @@
+"""ctypes binding of libkvr.so (the C ABI declared in include/kvr.h).
+
+This module is the only place that touches the shared library.  It fails
+loudly when the library is missing or when a tensor is not on a CUDA device:
+there is no CPU fallback for any operation of the package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, Structure, c_int, c_int64, c_size_t, c_void_p, c_char_p
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("KVR_LIB", _PKG / "libkvr.so"))
+
+KVR_OK = 0
+KVR_ERR_INVALID_ARGUMENT = 1
+KVR_ERR_UNSUPPORTED = 2
+KVR_ERR_MISALIGNED = 3
+KVR_ERR_CUDA = 4
+KVR_ERR_CAPACITY = 5
+KVR_ERR_WORKSPACE = 6
+KVR_MAX_LAYERS = 32
+
+# Every symbol include/kvr.h declares; tests check the library exports them.
+EXPORTED_SYMBOLS = (
+    "kvr_version",
+    "kvr_status_string",
+    "kvr_last_error",
+    "kvr_pack_unsigned",
+    "kvr_unpack_unsigned",
+    "kvr_quantize_per_token",
+    "kvr_quantize_grouped",
+    "kvr_dequantize",
+    "kvr_append",
+    "kvr_flush_groups",
+    "kvr_decode_plan",
+    "kvr_decode_attention",
+    "kvr_lse_merge",
+    "kvr_decode_partial",
+)
+
+
+class KvrError(RuntimeError):
+    """A libkvr call returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int, text: str, cuda: str = "") -> None:
+        msg = f"{fn} failed: {text} (status {status})"
+        if cuda:
+            msg += f": {cuda}"
+        super().__init__(msg)
+        self.status = status
+
+
+class TokenQuantArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p), ("x_bh_stride", c_int64), ("x_row_stride", c_int64),
+        ("payload", c_void_p), ("payload_bh_stride", c_int64),
+        ("scale", c_void_p), ("offset", c_void_p), ("meta_bh_stride", c_int64),
+        ("bh", c_int), ("rows", c_int), ("row0", c_int), ("head_dim", c_int), ("bits", c_int),
+        ("codes_scratch", c_void_p),
+    ]
+
+
+class GroupQuantArgs(Structure):
+    _fields_ = [
+        ("x", c_void_p), ("x_bh_stride", c_int64), ("x_row_stride", c_int64),
+        ("payload", c_void_p), ("payload_bh_stride", c_int64),
+        ("scale", c_void_p), ("offset", c_void_p), ("meta_bh_stride", c_int64),
+        ("bh", c_int), ("groups", c_int), ("group0", c_int), ("group_size", c_int),
+        ("head_dim", c_int), ("bits", c_int),
+        ("codes_scratch", c_void_p),
+    ]
+
+
+class DequantArgs(Structure):
+    _fields_ = [
+        ("payload", c_void_p), ("payload_bh_stride", c_int64),
+        ("scale", c_void_p), ("offset", c_void_p), ("meta_bh_stride", c_int64),
+        ("residual", c_void_p), ("residual_bh_stride", c_int64),
+        ("out", c_void_p), ("out_dtype", c_int), ("bh", c_int), ("seq_len", c_int),
+        ("prefix_len", c_int), ("group_size", c_int), ("head_dim", c_int), ("bits", c_int),
+    ]
+
+
+class AppendArgs(Structure):
+    _fields_ = [
+        ("k", c_void_p), ("v", c_void_p),
+        ("key_residual", c_void_p), ("key_residual_bh_stride", c_int64),
+        ("value_payload", c_void_p), ("value_payload_bh_stride", c_int64),
+        ("value_scale", c_void_p), ("value_offset", c_void_p), ("value_meta_bh_stride", c_int64),
+        ("bh", c_int), ("n", c_int), ("seq_len", c_int), ("res_len", c_int),
+        ("res_capacity", c_int), ("seq_capacity", c_int), ("head_dim", c_int), ("value_bits", c_int),
+    ]
+
+
+class FlushArgs(Structure):
+    _fields_ = [
+        ("residual_in", c_void_p), ("residual_out", c_void_p), ("residual_bh_stride", c_int64),
+        ("key_payload", c_void_p), ("key_payload_bh_stride", c_int64),
+        ("key_scale", c_void_p), ("key_offset", c_void_p), ("key_meta_bh_stride", c_int64),
+        ("bh", c_int), ("res_len", c_int), ("groups", c_int), ("prefix_len", c_int),
+        ("prefix_capacity", c_int), ("group_size", c_int), ("head_dim", c_int), ("key_bits", c_int),
+    ]
+
+
+class LayerPtrs(Structure):
+    _fields_ = [
+        ("key_payload", c_void_p), ("key_scale", c_void_p), ("key_offset", c_void_p),
+        ("key_residual", c_void_p), ("value_payload", c_void_p), ("value_scale", c_void_p),
+        ("value_offset", c_void_p), ("query", c_void_p), ("out", c_void_p),
+    ]
+
+
+class DecodeArgs(Structure):
+    _fields_ = [
+        ("layers", POINTER(LayerPtrs)), ("n_layers", c_int),
+        ("batch", c_int), ("q_heads", c_int), ("kv_heads", c_int), ("head_dim", c_int),
+        ("seq_len", c_int), ("prefix_len", c_int), ("group_size", c_int),
+        ("key_bits", c_int), ("value_bits", c_int),
+        ("key_payload_bh_stride", c_int64), ("key_meta_bh_stride", c_int64),
+        ("key_residual_bh_stride", c_int64), ("value_payload_bh_stride", c_int64),
+        ("value_meta_bh_stride", c_int64),
+        ("split_tokens", c_int), ("num_sms", c_int),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("counters", c_void_p),
+    ]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load libkvr.so once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m kv_reduce_b200.build` "
+            "(kv_reduce_b200 has no CPU fallback)"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    lib.kvr_version.restype = c_int
+    lib.kvr_status_string.restype = c_char_p
+    lib.kvr_status_string.argtypes = [c_int]
+    lib.kvr_last_error.restype = c_char_p
+    lib.kvr_pack_unsigned.argtypes = [c_void_p, c_int64, c_int, c_void_p, c_void_p]
+    lib.kvr_unpack_unsigned.argtypes = [c_void_p, c_int64, c_int, c_void_p, c_void_p]
+    lib.kvr_quantize_per_token.argtypes = [POINTER(TokenQuantArgs), c_void_p]
+    lib.kvr_quantize_grouped.argtypes = [POINTER(GroupQuantArgs), c_void_p]
+    lib.kvr_dequantize.argtypes = [POINTER(DequantArgs), c_void_p]
+    lib.kvr_append.argtypes = [POINTER(AppendArgs), c_void_p]
+    lib.kvr_flush_groups.argtypes = [POINTER(FlushArgs), c_void_p]
+    lib.kvr_decode_plan.argtypes = [POINTER(DecodeArgs), POINTER(c_int), POINTER(c_size_t), POINTER(c_size_t)]
+    lib.kvr_decode_attention.argtypes = [POINTER(DecodeArgs), c_void_p]
+    lib.kvr_decode_partial.argtypes = [POINTER(DecodeArgs), c_int, c_int, c_void_p, c_void_p, c_void_p]
+    lib.kvr_lse_merge.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
+    for name in EXPORTED_SYMBOLS:
+        if name not in ("kvr_version", "kvr_status_string", "kvr_last_error"):
+            getattr(lib, name).restype = c_int
+    _lib = lib
+    return lib
+
+
+def check(fn: str, status: int) -> None:
+    if status == KVR_OK:
+        return
+    lib = load()
+    text = lib.kvr_status_string(status).decode()
+    cuda = lib.kvr_last_error().decode() if status == KVR_ERR_CUDA else ""
+    raise KvrError(fn, status, text, cuda)
+
+
+def call(fn: str, *args) -> None:
+    check(fn, getattr(load(), fn)(*args))
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    if t is None or t.numel() == 0:
+        return None
+    return t.data_ptr()
+
+
+def require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("kv_reduce_b200 operates on CUDA tensors only (no CPU fallback).")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("All tensors must be on the same CUDA device.")
+    if dev is None:
+        raise ValueError("No CUDA tensor given.")
+    return dev

@@ -1,0 +1,155 @@
+// Shared helpers for the packed draft-KV kernels (sm_100a).
+//
+// Never compile this project with --use_fast_math: the quantizer must
+// reproduce IEEE fp32 division and round-half-even exactly as
+// kv_reduce/packed_kv_cache.py:181-182 / :240-241 does through torch.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/kvr.h"
+
+namespace kvr {
+
+// ----------------------------------------------------------------- status
+// Records the CUDA error text of the last failing call on this host thread.
+void set_last_cuda_error(cudaError_t e);
+
+inline int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return KVR_ERR_CUDA;
+  }
+  return KVR_OK;
+}
+
+inline cudaStream_t as_stream(kvr_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------ bf16 bits
+// bf16 <-> fp32 on raw 16-bit patterns.  bf16 -> fp32 is exact; fp32 ->
+// bf16 rounds to nearest even like torch's Tensor.to(torch.bfloat16).
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  __nv_bfloat16 h = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+// Low / high bf16 of a packed 32-bit word as fp32.
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// ------------------------------------------------------------ quantizer
+// scale = max(max-min, 1e-8) / (2^bits-1), IEEE division
+// (packed_kv_cache.py:181 and :240).
+__device__ __forceinline__ float affine_scale(float mn, float mx, int bits) {
+  float range = __fsub_rn(mx, mn);
+  range = fmaxf(range, 1e-8f);
+  return __fdiv_rn(range, static_cast<float>((1 << bits) - 1));
+}
+// code = clamp(round_half_even((x - min) / scale), 0, 2^bits-1)
+// (packed_kv_cache.py:182 and :241).
+__device__ __forceinline__ uint32_t affine_code(float x, float mn, float scale, int bits) {
+  float q = rintf(__fdiv_rn(__fsub_rn(x, mn), scale));
+  q = fminf(fmaxf(q, 0.0f), static_cast<float>((1 << bits) - 1));
+  return static_cast<uint32_t>(q);
+}
+// dequant = code * scale + offset with two roundings, no FMA contraction
+// (packed_kv_cache.py:131 and :145).
+__device__ __forceinline__ float affine_dequant(uint32_t code, float scale, float offset) {
+  return __fadd_rn(__fmul_rn(static_cast<float>(code), scale), offset);
+}
+
+// Byte `byte_idx` of the LSB-first bitstream of `codes` (bits per code),
+// reading codes from `get(i)` for i in [0, n).  Works for any bits in 1..8.
+template <typename Get>
+__device__ __forceinline__ uint32_t stream_byte(int64_t byte_idx, int bits, int64_t n, Get get) {
+  const int64_t bit0 = byte_idx * 8;
+  int64_t i = bit0 / bits;
+  const int64_t bit_end = bit0 + 8;
+  uint32_t out = 0;
+  for (; i < n && i * bits < bit_end; ++i) {
+    const int64_t pos = i * bits - bit0;  // may be negative for the first code
+    uint32_t c = get(i) & ((1u << bits) - 1u);
+    if (pos >= 0) out |= c << pos;
+    else out |= c >> (-pos);
+  }
+  return out & 0xffu;
+}
+
+// ------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t x, uint32_t mask, uint32_t orv) {
+  uint32_t r;
+  // (x & mask) | orv  -> lop3 immediate 0xEA
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(r) : "r"(x), "r"(mask), "r"(orv));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(r) : "r"(x));
+  return r;
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A(16x16, row) * B(16x8, col) + D, fp16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Same with bf16 inputs (BF16 residual keys x BF16 query: exact products).
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+
+}  // namespace kvr

@@ -1,0 +1,274 @@
+"""Decode attention over bit-packed KV: the API of
+kv_reduce/triton_packed_kv_attention.py on sm_100a.
+
+``packed_kv_decode_attention`` keeps the reference signature, argument
+meaning and ``ValueError`` preconditions (triton_packed_kv_attention.py:284-314)
+and runs one CUDA launch (split-K decode + fused LSE merge) from libkvr.so.
+
+Differences from the reference, stated where a caller could notice them:
+  * bits: {2, 4, 8} are accepted (the reference: {4, 8});
+  * geometry the kernel is built for: head_dim in {64, 128}, group_size a
+    multiple of 16, at most 8 query heads per KV head, bf16 query and
+    residual (other geometries raise ValueError instead of running);
+  * ``split_tokens=0`` picks the split count for the GPU (the reference runs a
+    single-pass kernel for 0); a positive value is honoured as the split
+    size, rounded up to ``block_tokens`` and then to 32 tokens.  Results agree
+    with every split choice to fp32 rounding.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, List, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from .packed_kv_cache import PackedKVComponent, _bh_stride
+
+SUPPORTED_BITS = {2, 4, 8}
+SUPPORTED_HEAD_DIMS = {64, 128}
+MAX_GQA = 8
+
+
+def theoretical_attention_flops(query: torch.Tensor, seq_len: int) -> int:
+    """Dot-product + value-accumulation FLOPs of one decode query (:392-395)."""
+    batch, query_heads, _, head_dim = query.shape
+    return int(4 * batch * query_heads * seq_len * head_dim)
+
+
+def _validate(query: torch.Tensor, packed_keys: PackedKVComponent, packed_values: PackedKVComponent,
+              block_tokens: int) -> None:
+    # Reference preconditions, same order and messages (:293-314).
+    if not query.is_cuda:
+        raise ValueError("Packed attention requires a CUDA query tensor.")
+    if query.ndim != 4 or query.shape[-2] != 1:
+        raise ValueError("query must have shape [batch, query_heads, 1, head_dim].")
+    if packed_keys.layout != "per_channel_grouped_affine":
+        raise ValueError("keys must use the grouped per-channel affine layout.")
+    if packed_values.layout != "per_token_affine":
+        raise ValueError("values must use the per-token affine layout.")
+    if packed_keys.bits not in SUPPORTED_BITS or packed_values.bits not in SUPPORTED_BITS:
+        raise ValueError("The fused kernel supports only 2-, 4- and 8-bit K/V payloads.")
+    if tuple(packed_keys.shape) != tuple(packed_values.shape):
+        raise ValueError("Packed key and value shapes must match.")
+    if tuple(query.shape[:1]) != tuple(packed_keys.shape[:1]):
+        raise ValueError("Query and cache batch dimensions must match.")
+    if query.shape[-1] != packed_keys.shape[-1]:
+        raise ValueError("Query and cache head dimensions must match.")
+    if query.shape[1] % packed_keys.shape[1] != 0:
+        raise ValueError("Query heads must be divisible by KV heads.")
+    if packed_keys.prefix_length <= 0:
+        raise ValueError("The fused kernel requires a non-empty quantized key prefix.")
+    if block_tokens not in {16, 32, 64}:
+        raise ValueError("block_tokens must be one of 16, 32, or 64.")
+    # Geometry this build's kernel covers.
+    if len(packed_keys.shape) != 4:
+        raise ValueError("packed K/V must have shape [batch, kv_heads, tokens, head_dim].")
+    head_dim = int(packed_keys.shape[-1])
+    if head_dim not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"head_dim must be one of {sorted(SUPPORTED_HEAD_DIMS)}.")
+    if head_dim == 64 and packed_values.bits == 2:
+        raise ValueError("2-bit values need head_dim 128.")
+    if query.shape[1] // packed_keys.shape[1] > MAX_GQA:
+        raise ValueError(f"At most {MAX_GQA} query heads per KV head are supported.")
+    if packed_keys.group_size % 16 != 0:
+        raise ValueError("group_size must be a multiple of 16 for the fused kernel.")
+    if query.dtype != torch.bfloat16:
+        raise ValueError("query must be bf16.")
+
+
+@dataclass(frozen=True)
+class CacheGeometry:
+    batch: int
+    q_heads: int
+    kv_heads: int
+    head_dim: int
+    seq_len: int
+    prefix_len: int
+    group_size: int
+    key_bits: int
+    value_bits: int
+    kp_bh: int
+    km_bh: int
+    kr_bh: int
+    vp_bh: int
+    vm_bh: int
+
+
+def _geometry(query: torch.Tensor, k: PackedKVComponent, v: PackedKVComponent) -> CacheGeometry:
+    batch, kv_heads, seq_len, head_dim = (int(s) for s in k.shape)
+    P = int(k.prefix_length)
+    kb, vb = int(k.bits), int(v.bits)
+    for t, what in ((k.scale, "key scale"), (k.offset, "key offset"), (v.scale, "value scale"),
+                    (v.offset, "value offset")):
+        if t is None or t.dtype != torch.bfloat16:
+            raise ValueError(f"{what} must be bf16.")
+    kp_bh = _bh_stride(k.payload, P * head_dim * kb // 8, "key payload")
+    km_bh = _bh_stride(k.scale, (P // k.group_size) * head_dim, "key scale")
+    if _bh_stride(k.offset, (P // k.group_size) * head_dim, "key offset") != km_bh:
+        raise ValueError("key scale and offset must share strides.")
+    kr_bh = 0
+    if seq_len > P:
+        if k.residual is None or k.residual.dtype != torch.bfloat16:
+            raise ValueError("key residual must be bf16.")
+        kr_bh = _bh_stride(k.residual, (seq_len - P) * head_dim, "key residual")
+    vp_bh = _bh_stride(v.payload, seq_len * head_dim * vb // 8, "value payload")
+    vm_bh = _bh_stride(v.scale, seq_len, "value scale")
+    if _bh_stride(v.offset, seq_len, "value offset") != vm_bh:
+        raise ValueError("value scale and offset must share strides.")
+    return CacheGeometry(batch, int(query.shape[1]), kv_heads, head_dim, seq_len, P, int(k.group_size),
+                         kb, vb, kp_bh, km_bh, kr_bh, vp_bh, vm_bh)
+
+
+def _layer_ptrs(query: torch.Tensor, out: torch.Tensor, k: PackedKVComponent,
+                v: PackedKVComponent) -> _lib.LayerPtrs:
+    res = k.residual if (k.residual is not None and k.residual.numel()) else None
+    return _lib.LayerPtrs(
+        _lib.ptr(k.payload), _lib.ptr(k.scale), _lib.ptr(k.offset), _lib.ptr(res),
+        _lib.ptr(v.payload), _lib.ptr(v.scale), _lib.ptr(v.offset), query.data_ptr(), out.data_ptr(),
+    )
+
+
+# Split-merge counters: zero on entry, left zero by every completed launch,
+# so one array per (device, stream) serves all launches on that stream.
+_COUNTERS: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def _counters(device: torch.device, stream: int, n: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+    buf = _COUNTERS.get(key)
+    if buf is None or buf.numel() < n:
+        buf = torch.zeros(max(n, 1024), dtype=torch.int32, device=device)
+        _COUNTERS[key] = buf
+    return buf
+
+
+class DecodeLaunch:
+    """A prepared decode launch over one or more layers of equal geometry.
+
+    Holds the ctypes argument block, the split plan and the workspace, so a
+    repeated call (a decode loop, a benchmark, a CUDA-graph capture) costs
+    one C call.  Pointers are fixed at construction: the tensors must stay
+    alive and in place.
+    """
+
+    def __init__(self, geom: CacheGeometry, layers: Sequence[_lib.LayerPtrs], device: torch.device,
+                 split_tokens: int = 0, stream: int | None = None,
+                 token_begin: int = 0, token_end: int | None = None) -> None:
+        if not 1 <= len(layers) <= _lib.KVR_MAX_LAYERS:
+            raise ValueError(f"1..{_lib.KVR_MAX_LAYERS} layers per launch.")
+        self.geom = geom
+        self.device = device
+        self.stream = _lib.stream_ptr(device) if stream is None else stream
+        self._layers = (_lib.LayerPtrs * len(layers))(*layers)
+        a = _lib.DecodeArgs()
+        a.layers = ctypes.cast(self._layers, ctypes.POINTER(_lib.LayerPtrs))
+        a.n_layers = len(layers)
+        a.batch, a.q_heads, a.kv_heads, a.head_dim = geom.batch, geom.q_heads, geom.kv_heads, geom.head_dim
+        a.seq_len, a.prefix_len, a.group_size = geom.seq_len, geom.prefix_len, geom.group_size
+        a.key_bits, a.value_bits = geom.key_bits, geom.value_bits
+        a.key_payload_bh_stride, a.key_meta_bh_stride = geom.kp_bh, geom.km_bh
+        a.key_residual_bh_stride, a.value_payload_bh_stride = geom.kr_bh, geom.vp_bh
+        a.value_meta_bh_stride = geom.vm_bh
+        a.split_tokens = int(split_tokens)
+        a.num_sms = torch.cuda.get_device_properties(device).multi_processor_count
+        ns, wsb, ncnt = ctypes.c_int(0), ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.check("kvr_decode_plan", _lib.load().kvr_decode_plan(a, ctypes.byref(ns), ctypes.byref(wsb),
+                                                                 ctypes.byref(ncnt)))
+        self.num_splits = ns.value
+        self.workspace = torch.empty(max(int(wsb.value), 16), dtype=torch.uint8, device=device)
+        self.counters = _counters(device, self.stream, int(ncnt.value))
+        a.workspace, a.workspace_bytes = self.workspace.data_ptr(), int(wsb.value)
+        a.counters = self.counters.data_ptr()
+        self.args = a
+        self.token_begin = int(token_begin)
+        self.token_end = geom.seq_len if token_end is None else int(token_end)
+
+    def __call__(self) -> None:
+        _lib.check("kvr_decode_attention", _lib.load().kvr_decode_attention(self.args, self.stream))
+
+    def partial(self, part_ml: torch.Tensor, part_o: torch.Tensor) -> None:
+        """Unnormalised (m, l, o) over tokens [token_begin, token_end)."""
+        _lib.check("kvr_decode_partial", _lib.load().kvr_decode_partial(
+            self.args, self.token_begin, self.token_end, part_ml.data_ptr(), part_o.data_ptr(), self.stream))
+
+
+def _effective_split(split_tokens: int, block_tokens: int) -> int:
+    if split_tokens <= 0:
+        return 0
+    return -(-int(split_tokens) // int(block_tokens)) * int(block_tokens)
+
+
+def packed_kv_decode_attention(
+    query: torch.Tensor,
+    packed_keys: PackedKVComponent,
+    packed_values: PackedKVComponent,
+    *,
+    block_tokens: int = 32,
+    split_tokens: int = 0,
+) -> torch.Tensor:
+    """One-token GQA attention straight from the packed cache.
+
+    Drop-in for triton_packed_kv_attention.packed_kv_decode_attention
+    (:284-389): returns a tensor like ``query``.
+    """
+    _validate(query, packed_keys, packed_values, block_tokens)
+    query = query.contiguous()
+    geom = _geometry(query, packed_keys, packed_values)
+    out = torch.empty_like(query)
+    launch = DecodeLaunch(geom, [_layer_ptrs(query, out, packed_keys, packed_values)], query.device,
+                          split_tokens=_effective_split(split_tokens, block_tokens))
+    launch()
+    return out
+
+
+def packed_kv_decode_attention_layers(
+    queries: Sequence[torch.Tensor],
+    packed_keys: Sequence[PackedKVComponent],
+    packed_values: Sequence[PackedKVComponent],
+    *,
+    split_tokens: int = 0,
+) -> List[torch.Tensor]:
+    """Decode attention for several layers of equal geometry in one launch.
+
+    Each layer is independent (its own query, cache and output); the result
+    equals calling packed_kv_decode_attention per layer.
+    """
+    if not (len(queries) == len(packed_keys) == len(packed_values)) or not queries:
+        raise ValueError("queries, packed_keys and packed_values must be non-empty and equally long.")
+    outs, ptrs, geom = [], [], None
+    for q, k, v in zip(queries, packed_keys, packed_values):
+        _validate(q, k, v, 32)
+        q = q.contiguous()
+        g = _geometry(q, k, v)
+        if geom is None:
+            geom = g
+        elif g != geom:
+            raise ValueError("All layers of one launch must share geometry and strides.")
+        o = torch.empty_like(q)
+        outs.append(o)
+        ptrs.append(_layer_ptrs(q, o, k, v))
+    out_all: List[torch.Tensor] = []
+    for start in range(0, len(ptrs), _lib.KVR_MAX_LAYERS):
+        DecodeLaunch(geom, ptrs[start:start + _lib.KVR_MAX_LAYERS], queries[0].device, split_tokens=split_tokens)()
+    out_all.extend(outs)
+    return out_all
+
+
+def lse_merge(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge per-shard partials: part_ml [n_parts, rows, 2] (m in log2 units, l),
+    part_o [n_parts, rows, D] -> bf16 [rows, D]."""
+    if part_ml.dim() != 3 or part_ml.shape[-1] != 2 or part_o.dim() != 3:
+        raise ValueError("part_ml must be [n_parts, rows, 2] and part_o [n_parts, rows, D].")
+    n_parts, rows, head_dim = (int(s) for s in part_o.shape)
+    if tuple(part_ml.shape[:2]) != (n_parts, rows):
+        raise ValueError("part_ml and part_o disagree on [n_parts, rows].")
+    dev = _lib.require_cuda(part_ml, part_o)
+    part_ml = part_ml.float().contiguous()
+    part_o = part_o.float().contiguous()
+    if out is None:
+        out = torch.empty(rows, head_dim, dtype=torch.bfloat16, device=dev)
+    _lib.call("kvr_lse_merge", part_ml.data_ptr(), part_o.data_ptr(), n_parts, rows, head_dim, out.data_ptr(),
+              _lib.stream_ptr(dev))
+    return out

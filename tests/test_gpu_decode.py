@@ -1,0 +1,185 @@
+"""GPU parity of the split-K packed decode attention against the oracle.
+
+Tolerance (floating point, stated by the path's spec): max |err| <= 2e-3 and
+mean |err| <= 1e-3 against the fp32 dequantize + softmax attention of the
+reference, computed by the oracle in float64.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_from_bits, bits_of
+from oracle import attention, packing
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS = 2e-3, 1e-3
+
+
+@pytest.fixture(scope="module")
+def kvr(built_lib):
+    import kv_reduce_b200
+
+    return kv_reduce_b200
+
+
+def oracle_out(keys, values, query, kb, vb, G, R):
+    kq = packing.quantize_grouped(bits_of(keys), kb, G, R)
+    vq = packing.quantize_per_token(bits_of(values), vb)
+    K = packing.dequant_grouped(kq["payload"], kq["scale"], kq["offset"], kq["residual"], kb, tuple(keys.shape),
+                                kq["P"], G)
+    V = packing.dequant_per_token(vq["payload"], vq["scale"], vq["offset"], vb, tuple(values.shape))
+    q = packing.bf16_to_f32(bits_of(query))[:, :, 0, :]
+    return attention.decode_attention(q, K, V)
+
+
+def check(out, ref, what=""):
+    got = out.float().cpu().numpy()[:, :, 0, :]
+    err = np.abs(got - ref)
+    assert err.max() <= MAX_ABS, f"{what}: max abs err {err.max():.3e}"
+    assert err.mean() <= MEAN_ABS, f"{what}: mean abs err {err.mean():.3e}"
+    return err
+
+
+def make(shape, hq, kb, vb, G, R, seed, q_scale=1.0, outliers=4):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    B, H, S, D = shape
+    k = torch.randn(shape, generator=g, device="cuda")
+    chans = torch.randperm(D, generator=torch.Generator().manual_seed(seed))[:outliers]
+    k[..., chans] *= 10
+    v = torch.randn(shape, generator=g, device="cuda")
+    q = torch.randn(B, hq, 1, D, generator=g, device="cuda") * q_scale
+    return k.to(torch.bfloat16), v.to(torch.bfloat16), q.to(torch.bfloat16)
+
+
+def test_golden_attention(kvr, golden):
+    """Kernel vs the reference's own fp32 unpack + SDPA result."""
+    for name in (str(c) for c in golden["kv_cases"]):
+        p = f"kv_{name}_"
+        if p + "query" not in golden.files:
+            continue
+        kb, vb, G, R, P = (int(v) for v in golden[p + "params"])
+        keys, values = bf16_from_bits(golden[p + "keys"]), bf16_from_bits(golden[p + "values"])
+        q = bf16_from_bits(golden[p + "query"])
+        pk, pv = kvr.pack_kivi_kv(keys, values, k_bits=kb, v_bits=vb, group_size=G, residual_length=R)
+        out = kvr.packed_kv_decode_attention(q, pk, pv)
+        assert out.shape == q.shape and out.dtype == q.dtype
+        check(out, golden[p + "attn_f32"][:, :, 0, :], name)
+
+
+@pytest.mark.parametrize("split", [0, 32, 64, 96, 512, 1 << 20])
+def test_config1_all_splits(kvr, split):
+    from kv_reduce_b200 import workloads
+
+    wl = workloads.CONFIGS["1"]
+    k, v = workloads.make_layer_kv(wl, 0)
+    q = workloads.make_query(wl, 0)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=0)
+    out = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=split)
+    check(out, oracle_out(k, v, q, 4, 4, 32, 0), f"split={split}")
+
+
+@pytest.mark.parametrize("shape,hq,kb,vb,G,R", [
+    ((1, 2, 1026, 128), 12, 4, 4, 32, 0),     # after crop in the reference unit test
+    ((1, 2, 1057, 128), 12, 4, 4, 32, 128),   # group boundary + residual
+    ((2, 2, 4099, 128), 12, 2, 2, 32, 128),   # K2V2 ragged
+    ((2, 2, 2000, 128), 12, 8, 4, 32, 128),
+    ((2, 2, 2000, 128), 12, 4, 8, 32, 128),
+    ((1, 2, 777, 128), 12, 8, 8, 16, 64),     # G=16: two groups per chunk
+    ((1, 2, 777, 128), 16, 4, 2, 64, 33),     # GQA 8, G=64, odd residual
+    ((3, 8, 1500, 64), 32, 8, 4, 32, 128),    # Llama geometry, K8V4
+    ((3, 8, 1500, 64), 32, 4, 8, 32, 128),    # K4V8
+    ((1, 4, 300, 64), 4, 2, 4, 32, 0),        # GQA 1
+    ((1, 2, 33, 128), 12, 4, 4, 32, 0),       # one group + 1 residual token
+])
+def test_shapes_match_oracle(kvr, shape, hq, kb, vb, G, R):
+    k, v, q = make(shape, hq, kb, vb, G, R, seed=sum(shape) + kb + vb + G + R)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=kb, v_bits=vb, group_size=G, residual_length=R)
+    ref = oracle_out(k, v, q, kb, vb, G, R)
+    for split in (0, 64):
+        out = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=split)
+        check(out, ref, f"{shape} k{kb}v{vb} G{G} R{R} split={split}")
+
+
+def test_peaked_attention(kvr):
+    """A query 6x larger: near one-hot softmax, largest fp16 operand rounding."""
+    k, v, q = make((1, 2, 2048, 128), 12, 4, 4, 32, 128, seed=99, q_scale=6.0)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+    out = kvr.packed_kv_decode_attention(q, pk, pv)
+    check(out, oracle_out(k, v, q, 4, 4, 32, 128), "peaked")
+
+
+def test_full_size_config2_layer(kvr):
+    """One full 32K-token layer, checked against the oracle."""
+    from kv_reduce_b200 import workloads
+
+    wl = workloads.CONFIGS["2"]
+    k, v = workloads.make_layer_kv(wl, 3)
+    q = workloads.make_query(wl, 3)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+    out = kvr.packed_kv_decode_attention(q, pk, pv)
+    check(out, oracle_out(k, v, q, 4, 4, 32, 128), "32K")
+    # the reference's own launch choice (split 512, block 32) gives the same result
+    out512 = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=512)
+    assert (out512.float() - out.float()).abs().max().item() <= 2e-3
+
+
+def test_multi_layer_launch_equals_per_layer(kvr):
+    from kv_reduce_b200 import workloads
+
+    wl = workloads.CONFIGS["2"].scaled(seq_len=3000, layers=5)
+    qs, ks, vs = [], [], []
+    for layer in range(wl.layers):
+        k, v = workloads.make_layer_kv(wl, layer)
+        pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+        qs.append(workloads.make_query(wl, layer))
+        ks.append(pk)
+        vs.append(pv)
+    outs = kvr.packed_kv_decode_attention_layers(qs, ks, vs)
+    for q, pk, pv, o in zip(qs, ks, vs, outs):
+        single = kvr.packed_kv_decode_attention(q, pk, pv)
+        assert torch.equal(single, o)
+
+
+def test_token_shards_merge_to_full(kvr):
+    """Partial decode over token shards + LSE merge == full decode (the
+    cross-GPU split of one long sequence, emulated on one GPU)."""
+    from kv_reduce_b200.packed_kv_attention import DecodeLaunch, _geometry, _layer_ptrs, lse_merge
+
+    k, v, q = make((1, 2, 5000, 128), 12, 4, 4, 32, 128, seed=5)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+    full = kvr.packed_kv_decode_attention(q, pk, pv)
+    geom = _geometry(q, pk, pv)
+    bounds = [0, 1024, 2048, 4096, 5000]
+    mls, os_ = [], []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        ml = torch.empty(12, 2, device="cuda")
+        o = torch.empty(12, 128, device="cuda")
+        dummy = torch.empty_like(q)
+        DecodeLaunch(geom, [_layer_ptrs(q, dummy, pk, pv)], q.device, token_begin=a, token_end=b).partial(ml, o)
+        mls.append(ml)
+        os_.append(o)
+    merged = lse_merge(torch.stack(mls), torch.stack(os_)).reshape(1, 12, 1, 128)
+    assert (merged.float() - full.float()).abs().max().item() <= 2e-3
+    check(merged, oracle_out(k, v, q, 4, 4, 32, 128), "shards")
+
+
+def test_api_errors(kvr):
+    k, v, q = make((1, 2, 256, 128), 12, 4, 4, 32, 0, seed=1)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=0)
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q.cpu(), pk, pv)
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q[:, :, :, :64], pk, pv)
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q, pv, pk)
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q, pk, pv, block_tokens=48)
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q[:, :11], pk, pv)
+    empty_k, empty_v = kvr.pack_kivi_kv(k[:, :, :100], v[:, :, :100], k_bits=4, v_bits=4, residual_length=128)
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q, empty_k, empty_v)
+    k3, v3 = kvr.pack_kivi_kv(k, v, k_bits=3, v_bits=4, group_size=32, residual_length=0)
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q, k3, v3)
