@@ -157,7 +157,7 @@ int kvr_flush_groups(const kvr_flush_args* a, kvr_stream_t stream);
  * over the packed cache, split-K over tokens, online softmax in fp32, LSE
  * merge of the splits fused into the same launch.  Several layers of equal
  * geometry may share one launch (n_layers <= KVR_MAX_LAYERS).
- * query/out: [B, HQ, 1, D] bf16 contiguous per layer.
+ * query: [B, HQ, 1, D] bf16, out: [B, HQ, 1, D] bf16 or fp32, contiguous.
  * Supported: D in {64,128}; key/value bits in {2,4,8} (D=64 needs value
  * bits >= 4); G a multiple of 16 with G <= 128 or G == 16*k; HQ/HKV <= 8.
  * The caller passes a workspace of kvr_decode_plan() bytes for the split
@@ -173,7 +173,7 @@ typedef struct {
   const uint16_t* value_scale;
   const uint16_t* value_offset;
   const uint16_t* query;
-  uint16_t* out;
+  void* out;            /* bf16 or fp32, see kvr_decode_args.out_dtype */
 } kvr_layer_ptrs;
 
 typedef struct {
@@ -186,6 +186,7 @@ typedef struct {
   int64_t key_residual_bh_stride;  /* elements */
   int64_t value_payload_bh_stride; /* bytes    */
   int64_t value_meta_bh_stride;    /* elements */
+  int out_dtype;      /* 0: bf16 output (the query dtype), 1: fp32 output */
   int split_tokens;   /* > 0: tokens per split (rounded up to 32); 0: auto */
   int num_sms;        /* 0: query the current device */
   void* workspace; size_t workspace_bytes;   /* split partials */

@@ -124,7 +124,7 @@ class DecodeArgs(Structure):
         ("key_payload_bh_stride", c_int64), ("key_meta_bh_stride", c_int64),
         ("key_residual_bh_stride", c_int64), ("value_payload_bh_stride", c_int64),
         ("value_meta_bh_stride", c_int64),
-        ("split_tokens", c_int), ("num_sms", c_int),
+        ("out_dtype", c_int), ("split_tokens", c_int), ("num_sms", c_int),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("counters", c_void_p),
     ]

@@ -150,6 +150,21 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+// 2^x with the hardware approximation (ex2.approx.ftz: ~2 ulp; inputs here
+// are x <= 0 from the online softmax, tiny results flush to zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Exact product split in fp16x2 (TwoProduct with a fused multiply-add):
+// hi = fl(a*b), lo = fma(a, b, -hi); hi + lo == a*b exactly unless the
+// error term falls into the fp16 subnormal range.
+__device__ __forceinline__ void two_prod_h2(uint32_t a, uint32_t b, uint32_t& hi, uint32_t& lo) {
+  asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(hi) : "r"(a), "r"(b));
+  const uint32_t nhi = hi ^ 0x80008000u;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(lo) : "r"(a), "r"(b), "r"(nhi));
+}
 
 }  // namespace kvr

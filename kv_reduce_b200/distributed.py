@@ -1,0 +1,136 @@
+"""Multi-GPU layouts of the packed decode path (one process per GPU).
+
+Two partitions, both from the build's partitioning of batch x KV-head x
+tokens:
+
+* batch sharding (weak scaling): each rank owns whole sequences; decode is
+  rank-local and needs no collective.  ``batch_shard`` picks a rank's slice.
+* sequence split (one long sequence, batch 1): each rank owns a contiguous,
+  32-token-aligned range of every layer's tokens.  A step is a partial
+  decode per rank -- unnormalised (m, l, o) per query head, m in log2 units
+  -- an all-gather of those partials (NCCL over NVLink, a few KB per
+  layer), and an LSE merge.  ``shard_component`` cuts a rank's token range
+  out of a packed component; ``SequenceShardDecoder`` runs the step.
+
+The reference has no multi-GPU path (its only multi-device use places the
+target and draft models on different GPUs,
+kv_reduce/experiments/benchmark_spec_kv_quantization.py:1157-1158).
+"""
+from __future__ import annotations
+
+from typing import Callable, List, Tuple
+
+import torch
+
+from .packed_kv_cache import PackedKVComponent
+
+CHUNK = 32
+
+
+def batch_shard(batch: int, world: int, rank: int) -> Tuple[int, int]:
+    """[begin, end) of the sequences rank `rank` owns (near-equal split)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad world/rank")
+    base, extra = divmod(batch, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+def token_shards(seq_len: int, world: int, align: int = CHUNK) -> List[Tuple[int, int]]:
+    """Contiguous token ranges, boundaries multiples of `align`, the last
+    range ending at seq_len.  Ranks past the end get empty ranges."""
+    if world < 1 or align < 1:
+        raise ValueError("bad world/align")
+    units = -(-seq_len // align)
+    out = []
+    for r in range(world):
+        a = (units * r // world) * align
+        b = min(seq_len, (units * (r + 1) // world) * align)
+        out.append((min(a, seq_len), max(min(a, seq_len), b)))
+    return out
+
+
+def shard_component(k: PackedKVComponent, v: PackedKVComponent, begin: int, end: int
+                    ) -> Tuple[PackedKVComponent, PackedKVComponent]:
+    """Tokens [begin, end) of a packed (keys, values) pair as a compact pair.
+
+    `begin` must be a multiple of the key group size; the shard's quantized
+    prefix is the part of [begin, end) below the global prefix, and only a
+    shard reaching past the prefix holds BF16 residual rows.
+    """
+    B, H, S, D = (int(s) for s in k.shape)
+    G, P = int(k.group_size), int(k.prefix_length)
+    if not (0 <= begin < end <= S) or begin % G:
+        raise ValueError("shard bounds must satisfy 0 <= begin < end <= S with begin % group_size == 0")
+    if begin < P and end < P and end % G:
+        raise ValueError("a shard ending inside the prefix must end on a group boundary")
+    kb, vb = int(k.bits), int(v.bits)
+    p_end = min(end, P)
+    n_pref = max(0, p_end - begin)
+    rbk, rbv = D * kb // 8, D * vb // 8
+    kp = k.payload.reshape(B, H, P, rbk)[:, :, begin:begin + n_pref].contiguous().reshape(-1)
+    ks = k.scale.reshape(B, H, P // G, 1, D)[:, :, begin // G:(begin + n_pref) // G].contiguous()
+    ko = k.offset.reshape(B, H, P // G, 1, D)[:, :, begin // G:(begin + n_pref) // G].contiguous()
+    r0, r1 = max(begin, P) - P, max(end, P) - P
+    res = k.residual[:, :, r0:r1].contiguous() if k.residual is not None else None
+    vp = v.payload.reshape(B, H, S, rbv)[:, :, begin:end].contiguous().reshape(-1)
+    vs = v.scale.reshape(B, H, S, 1)[:, :, begin:end].contiguous()
+    vo = v.offset.reshape(B, H, S, 1)[:, :, begin:end].contiguous()
+    shape = (B, H, end - begin, D)
+    ks_out = PackedKVComponent(kp, ks, ko, res, shape, kb, k.layout, k.output_dtype, G, n_pref)
+    vs_out = PackedKVComponent(vp, vs, vo, None, shape, vb, v.layout, v.output_dtype)
+    return ks_out, vs_out
+
+
+def merge_partials(ml: torch.Tensor, o: torch.Tensor) -> torch.Tensor:
+    """Reference LSE merge on any device: ml [N, rows, 2], o [N, rows, D] -> [rows, D] fp32."""
+    m, l = ml[..., 0], ml[..., 1]
+    M = m.max(dim=0).values
+    w = torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp2(m - M))
+    L = (w * l).sum(0)
+    out = (w[..., None] * o).sum(0)
+    return torch.where(L[:, None] > 0, out / L.clamp_min(1e-30)[:, None], torch.zeros_like(out))
+
+
+class SequenceShardDecoder:
+    """One rank's side of a sequence-split decode step.
+
+    partial_fn() fills this rank's (ml [rows, 2], o [rows, D]) partials;
+    the step all-gathers them over the process group and merges them with
+    merge_fn (the GPU kvr_lse_merge kernel in production; the torch
+    reference merge in CPU tests).  Every rank takes the same collective
+    steps in the same order.
+    """
+
+    def __init__(self, rows: int, head_dim: int, world: int, device: torch.device,
+                 partial_fn: Callable[[torch.Tensor, torch.Tensor], None],
+                 merge_fn: Callable[[torch.Tensor, torch.Tensor], torch.Tensor] | None = None,
+                 group=None) -> None:
+        self.rows, self.head_dim, self.world = rows, head_dim, world
+        self.partial_fn = partial_fn
+        self.merge_fn = merge_fn or merge_partials
+        self.group = group
+        self.ml = torch.empty(rows, 2, dtype=torch.float32, device=device)
+        self.o = torch.empty(rows, head_dim, dtype=torch.float32, device=device)
+        self.ml_all = torch.empty(world, rows, 2, dtype=torch.float32, device=device)
+        self.o_all = torch.empty(world, rows, head_dim, dtype=torch.float32, device=device)
+
+    def step(self) -> torch.Tensor:
+        import torch.distributed as dist
+
+        self.partial_fn(self.ml, self.o)
+        if self.world > 1:
+            # list form: works on NCCL and gloo alike; the views land in place
+            dist.all_gather(list(self.ml_all.unbind(0)), self.ml, group=self.group)
+            dist.all_gather(list(self.o_all.unbind(0)), self.o, group=self.group)
+        else:
+            self.ml_all[0].copy_(self.ml)
+            self.o_all[0].copy_(self.o)
+        return self.merge_fn(self.ml_all, self.o_all)
+
+
+def empty_partial(ml: torch.Tensor, o: torch.Tensor) -> None:
+    """Partials of a rank that owns no tokens: no mass (m = -inf, l = 0)."""
+    ml[:, 0].fill_(float("-inf"))
+    ml[:, 1].zero_()
+    o.zero_()

@@ -155,7 +155,7 @@ class DecodeLaunch:
 
     def __init__(self, geom: CacheGeometry, layers: Sequence[_lib.LayerPtrs], device: torch.device,
                  split_tokens: int = 0, stream: int | None = None,
-                 token_begin: int = 0, token_end: int | None = None) -> None:
+                 token_begin: int = 0, token_end: int | None = None, out_fp32: bool = False) -> None:
         if not 1 <= len(layers) <= _lib.KVR_MAX_LAYERS:
             raise ValueError(f"1..{_lib.KVR_MAX_LAYERS} layers per launch.")
         self.geom = geom
@@ -171,6 +171,7 @@ class DecodeLaunch:
         a.key_payload_bh_stride, a.key_meta_bh_stride = geom.kp_bh, geom.km_bh
         a.key_residual_bh_stride, a.value_payload_bh_stride = geom.kr_bh, geom.vp_bh
         a.value_meta_bh_stride = geom.vm_bh
+        a.out_dtype = 1 if out_fp32 else 0
         a.split_tokens = int(split_tokens)
         a.num_sms = torch.cuda.get_device_properties(device).multi_processor_count
         ns, wsb, ncnt = ctypes.c_int(0), ctypes.c_size_t(0), ctypes.c_size_t(0)
@@ -207,18 +208,23 @@ def packed_kv_decode_attention(
     *,
     block_tokens: int = 32,
     split_tokens: int = 0,
+    out_dtype: torch.dtype | None = None,
 ) -> torch.Tensor:
     """One-token GQA attention straight from the packed cache.
 
     Drop-in for triton_packed_kv_attention.packed_kv_decode_attention
-    (:284-389): returns a tensor like ``query``.
+    (:284-389): returns a tensor like ``query``.  ``out_dtype=torch.float32``
+    (an addition) returns the fp32 result before the cast to the query dtype.
     """
     _validate(query, packed_keys, packed_values, block_tokens)
+    if out_dtype not in (None, query.dtype, torch.float32):
+        raise ValueError("out_dtype must be None, the query dtype or torch.float32.")
     query = query.contiguous()
     geom = _geometry(query, packed_keys, packed_values)
-    out = torch.empty_like(query)
+    out_fp32 = out_dtype == torch.float32
+    out = torch.empty(query.shape, dtype=torch.float32 if out_fp32 else query.dtype, device=query.device)
     launch = DecodeLaunch(geom, [_layer_ptrs(query, out, packed_keys, packed_values)], query.device,
-                          split_tokens=_effective_split(split_tokens, block_tokens))
+                          split_tokens=_effective_split(split_tokens, block_tokens), out_fp32=out_fp32)
     launch()
     return out
 

@@ -212,8 +212,9 @@ class PackedKVCacheLayer:
             layout="per_token_affine", output_dtype=torch.bfloat16,
         )
 
-    def attention(self, query: torch.Tensor, *, split_tokens: int = 0) -> torch.Tensor:
-        return packed_kv_decode_attention(query, self.k, self.v, split_tokens=split_tokens)
+    def attention(self, query: torch.Tensor, *, split_tokens: int = 0,
+                  out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        return packed_kv_decode_attention(query, self.k, self.v, split_tokens=split_tokens, out_dtype=out_dtype)
 
     def breakdown(self) -> Dict[str, int]:
         """Byte accounting with the keys of packed_review.py:50-54."""

@@ -42,8 +42,10 @@ def test_c_abi_validation_without_gpu(built_lib):
     a.num_sms = 148
     ns, ws, nc = ctypes.c_int(), ctypes.c_size_t(), ctypes.c_size_t()
     assert lib.kvr_decode_plan(a, ctypes.byref(ns), ctypes.byref(ws), ctypes.byref(nc)) == _lib.KVR_OK
-    assert 1 <= ns.value <= 256 and nc.value == 2
-    assert ws.value == (2 * ns.value * 8 * 130 * 4 if ns.value > 1 else 0)
+    assert 1 <= ns.value <= 256
+    g1 = -(-ns.value // 16)                       # first-level merge groups of 16 splits
+    assert nc.value == 2 * (g1 + 1)
+    assert ws.value == (2 * (ns.value + (g1 if g1 > 1 else 0)) * 8 * 130 * 4 if ns.value > 1 else 0)
     a.key_bits = 3
     assert lib.kvr_decode_plan(a, None, None, None) == _lib.KVR_ERR_UNSUPPORTED
     a.key_bits, a.head_dim = 4, 96
