@@ -199,6 +199,19 @@ int kvr_decode_plan(const kvr_decode_args* a, int* num_splits,
                     size_t* workspace_bytes, size_t* counter_count);
 int kvr_decode_attention(const kvr_decode_args* a, kvr_stream_t stream);
 
+/* Same as kvr_decode_attention for callers that cannot allocate device
+ * memory (an FFI host without a CUDA allocator, a serving loop that must not
+ * call cudaMalloc, a fixed memory budget).  No counterpart in the reference:
+ * its decode path always allocates its split buffers with torch.
+ * a->workspace and a->counters are ignored; the split scratch is a fixed
+ * 4 MiB array compiled into the library, held by every GPU that loads it.
+ * A problem whose plan needs more scratch than that returns
+ * KVR_ERR_WORKSPACE.  The first call on a device looks up the array's
+ * address (make it before any stream capture on that device).  Every call
+ * shares the array and clears its counters; calls that overlap on the GPU
+ * race.                                                                    */
+int kvr_decode_attention_noalloc(const kvr_decode_args* a, kvr_stream_t stream);
+
 /* LSE merge of externally produced partials (the cross-GPU token split):
  * parts: n_parts blocks of [rows] (m, l) pairs and [rows, D] unnormalised
  * outputs, m in log2 units; out[rows, D] bf16 = sum_p 2^(m_p-M) o_p /

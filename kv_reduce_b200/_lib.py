@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "kvr_decode_attention",
     "kvr_lse_merge",
     "kvr_decode_partial",
+    "kvr_decode_attention_noalloc",
 )
 
 
@@ -159,6 +160,7 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_attention.argtypes = [POINTER(DecodeArgs), c_void_p]
     lib.kvr_decode_partial.argtypes = [POINTER(DecodeArgs), c_int, c_int, c_void_p, c_void_p, c_void_p]
     lib.kvr_lse_merge.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
+    lib.kvr_decode_attention_noalloc.argtypes = [POINTER(DecodeArgs), c_void_p]
     for name in EXPORTED_SYMBOLS:
         if name not in ("kvr_version", "kvr_status_string", "kvr_last_error"):
             getattr(lib, name).restype = c_int

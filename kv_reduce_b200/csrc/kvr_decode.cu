@@ -1027,6 +1027,69 @@ extern "C" int kvr_decode_partial(const kvr_decode_args* a, int token_begin, int
   return dec::run(a, token_begin, token_end, part_ml, part_o, as_stream(stream));
 }
 
+// ---------------------------------------------------------------------------
+// Decode attention for callers that cannot allocate device memory.
+//
+// Some callers of this library have no device allocator to hand: an FFI host
+// (Go, Java, a C engine) that owns no CUDA memory pool, a real-time serving
+// loop that must not call cudaMalloc (it can synchronize the device and stall
+// every stream), or code running under a fixed memory budget.  They cannot
+// provide the split-partial workspace kvr_decode_attention asks for, so this
+// entry point keeps that scratch in a fixed array compiled into the library.
+//
+// The array is file-scope device memory: every GPU that loads the library
+// holds it until the process exits.  Host code cannot use the array's name
+// as a device address; its address is looked up once per device with
+// cudaGetSymbolAddress, with that device current, on the first call made on
+// that device -- so make the first call on each device before any stream
+// capture.  All calls share the array and it keeps the last call's contents:
+// each call clears the split counters it uses, and two calls that overlap on
+// the GPU (different streams, or concurrent graph launches) race.
+namespace kvr {
+namespace dec {
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;   // 4 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static void* g_noalloc_base[64];   // device address of the array, per device ordinal
+
+static int noalloc_base(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
+  if (dev < 0 || dev >= 64) return KVR_ERR_UNSUPPORTED;
+  if (!g_noalloc_base[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
+    g_noalloc_base[dev] = p;
+  }
+  *out = g_noalloc_base[dev];
+  return KVR_OK;
+}
+}  // namespace dec
+}  // namespace kvr
+
+extern "C" int kvr_decode_attention_noalloc(const kvr_decode_args* a, kvr_stream_t stream) {
+  if (!a) return KVR_ERR_INVALID_ARGUMENT;
+  dec::Plan pl;
+  int st = dec::run(a, 0, a->seq_len, nullptr, nullptr, nullptr, &pl);   // validates, plans
+  if (st != KVR_OK) return st;
+  const size_t counter_bytes = (pl.counters * sizeof(int) + 255) / 256 * 256;
+  if (counter_bytes + pl.part_bytes > dec::kNoAllocScratchBytes) return KVR_ERR_WORKSPACE;
+  void* base = nullptr;
+  st = dec::noalloc_base(&base);
+  if (st != KVR_OK) return st;
+  kvr_decode_args b = *a;
+  b.counters = static_cast<int*>(base);
+  b.workspace = static_cast<unsigned char*>(base) + counter_bytes;
+  b.workspace_bytes = dec::kNoAllocScratchBytes - counter_bytes;
+  if (pl.num_splits > 1) {
+    // the array keeps the previous call's contents: counters must start at zero
+    cudaError_t e = cudaMemsetAsync(b.counters, 0, pl.counters * sizeof(int), as_stream(stream));
+    if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
+  }
+  return dec::run(&b, 0, a->seq_len, nullptr, nullptr, as_stream(stream));
+}
+
 extern "C" int kvr_lse_merge(const float* part_ml, const float* part_o, int n_parts, int rows, int head_dim,
                              uint16_t* out, kvr_stream_t stream) {
   if (!part_ml || !part_o || !out || n_parts < 1 || rows < 0 || head_dim < 1) return KVR_ERR_INVALID_ARGUMENT;
