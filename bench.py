@@ -6,9 +6,11 @@ One step = decode attention for every layer of the workload's packed cache
 K4V4, key group 32, 128-token BF16 residual window, batch 1).
 
   value  : achieved algorithmic HBM GB/s of the step (all ranks), inputs
-           resident in HBM, the 28 per-layer launches replayed as one CUDA
-           graph.  Layers rotate through 273 MB of distinct buffers, more
-           than the 126 MB L2, so no flush is needed.
+           resident in HBM, all layers of the step in one launch (layer
+           index in the grid), replayed as a CUDA graph.  Layers rotate
+           through 273 MB of distinct buffers, more than the 126 MB L2, so
+           no flush is needed.  `per_layer` times the same step as one
+           launch per layer (28 launches in a CUDA graph).
   e2e    : the same metric through the public Python API with the queries
            copied host->device and the outputs device->host every step.
 
@@ -50,6 +52,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--split-sequence", action="store_true",
+                   help="N>1: split ONE batch-1 sequence's tokens across the ranks (strong scaling, "
+                        "partial decode + NCCL all-gather + LSE merge) instead of one sequence per rank")
     return p.parse_args()
 
 
@@ -290,43 +295,57 @@ def run_ours(args, wl, world, rank, local):
     outs = [torch.empty_like(q) for q in qs]
     geom = _geometry(qs[0], ks[0], vs[0])
     stream = torch.cuda.Stream(device)
-    per_layer = [DecodeLaunch(geom, [_layer_ptrs(q, o, k, v)], device, split_tokens=args.split_tokens,
-                              stream=stream.cuda_stream) for q, o, k, v in zip(qs, outs, ks, vs)]
-    fused = [DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, outs, ks, vs)][i:i + 32],
-                          device, split_tokens=args.split_tokens, stream=stream.cuda_stream)
+    ptrs = [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, outs, ks, vs)]
+    # the whole step in one launch per <= 32 layers (layer index in the grid)
+    fused = [DecodeLaunch(geom, ptrs[i:i + 32], device, split_tokens=args.split_tokens, stream=stream.cuda_stream)
              for i in range(0, wl.layers, 32)]
+    # one launch per layer, as a model calls it
+    per_layer = [DecodeLaunch(geom, [p], device, split_tokens=args.split_tokens, stream=stream.cuda_stream)
+                 for p in ptrs]
     torch.cuda.synchronize()
     lb = workloads.layer_bytes(wl)
     step_bytes = lb["total"] * wl.layers
-
-    def step_per_layer():
-        for launch in per_layer:
-            launch()
 
     def step_fused():
         for launch in fused:
             launch()
 
-    with ClockSampler(device) as clocks:
-        ms_layers = time_graph(step_per_layer, stream, args.steps, args.warmup, world, pg_sync)
-    ms_layers = max_over_ranks(ms_layers, world, device)
-    ms_fused = max_over_ranks(time_graph(step_fused, stream, args.steps, args.warmup, world, pg_sync), world, device)
+    def step_per_layer():
+        for launch in per_layer:
+            launch()
 
-    step_ms = ms_layers / args.steps
+    with ClockSampler(device) as clocks:
+        ms_fused = time_graph(step_fused, stream, args.steps, args.warmup, world, pg_sync)
+    ms_fused = max_over_ranks(ms_fused, world, device)
+    ms_layers = max_over_ranks(time_graph(step_per_layer, stream, args.steps, args.warmup, world, pg_sync),
+                               world, device)
+
+    step_ms = ms_fused / args.steps
     value = step_bytes * world / (step_ms * 1e-3) / 1e9
-    fused_step_ms = ms_fused / args.steps
+    layer_step_ms = ms_layers / args.steps
     peak, peak_src = measured_peak()
-    launch_us = step_ms * 1e3 / wl.layers
-    achieved = lb["total"] / (launch_us * 1e-6) / 1e9
+    launch_us = step_ms * 1e3 / len(fused)
+    bytes_per_launch = step_bytes / len(fused)
+    achieved = bytes_per_launch / (launch_us * 1e-6) / 1e9
 
     # ---------------------------------------------------------------- e2e
     e2e = None
+    e2e_per_layer = None
     if not args.no_e2e:
         q_host = [q.cpu().pin_memory() for q in qs]
         o_host = [torch.empty_like(h).pin_memory() for h in q_host]
         q_dev = [torch.empty_like(q) for q in qs]
+        io_bytes = sum(q.numel() * q.element_size() for q in qs)
 
-        def e2e_step():
+        def e2e_layers():
+            for i in range(wl.layers):
+                q_dev[i].copy_(q_host[i], non_blocking=True)
+            res = kvr.packed_kv_decode_attention_layers(q_dev, ks, vs, split_tokens=args.split_tokens)
+            for i in range(wl.layers):
+                o_host[i].copy_(res[i], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        def e2e_calls():
             res = []
             for i in range(wl.layers):
                 q_dev[i].copy_(q_host[i], non_blocking=True)
@@ -335,23 +354,29 @@ def run_ours(args, wl, world, rank, local):
                 o_host[i].copy_(res[i], non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
-        for _ in range(max(args.warmup, 3)):
-            e2e_step()
-        pg_sync()
-        t0 = time.perf_counter()
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(args.steps):
-            e2e_step()
-        s1.record()
-        torch.cuda.synchronize()
-        wall_ms = (time.perf_counter() - t0) * 1e3
-        e2e_ms = max(s0.elapsed_time(s1), wall_ms) / args.steps
-        e2e_ms = max_over_ranks(e2e_ms, world, device)
+        def time_host(fn):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            pg_sync()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            s0.record()
+            for _ in range(args.steps):
+                fn()
+            s1.record()
+            torch.cuda.synchronize()
+            wall_ms = (time.perf_counter() - t0) * 1e3
+            return max_over_ranks(max(s0.elapsed_time(s1), wall_ms) / args.steps, world, device)
+
+        e2e_ms = time_host(e2e_layers)
         e2e = {"value": step_bytes * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": sum(q.numel() * q.element_size() for q in qs),
-               "d2h_bytes_per_step": sum(q.numel() * q.element_size() for q in qs),
-               "ms_per_step": e2e_ms, "path": "kv_reduce_b200.packed_kv_decode_attention per layer, pinned host buffers"}
+               "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes, "ms_per_step": e2e_ms,
+               "path": "kv_reduce_b200.packed_kv_decode_attention_layers, queries H2D from pinned memory, "
+                       "outputs D2H, per step"}
+        e2e_pl_ms = time_host(e2e_calls)
+        e2e_per_layer = {"value": step_bytes * world / (e2e_pl_ms * 1e-3) / 1e9, "unit": "GB/s",
+                         "ms_per_step": e2e_pl_ms,
+                         "path": "kv_reduce_b200.packed_kv_decode_attention once per layer (the reference's call)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -362,33 +387,117 @@ def run_ours(args, wl, world, rank, local):
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "us_per_step": step_ms * 1e3,
             "tokens_per_s": wl.batch * world / (step_ms * 1e-3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes, fp16 mma, fp32 softmax",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u4 codes; f16/bf16 mma, fp32 accumulate and softmax",
             "data": "synthetic (seeded N(0,1) K/V/Q, outlier key channels)",
             "config": {"workload": wl.name, "layers": wl.layers, "batch_per_gpu": wl.batch,
                        "global_batch": wl.batch * world, "seq_len": wl.seq_len, "q_heads": wl.q_heads,
                        "kv_heads": wl.kv_heads, "head_dim": wl.head_dim, "kv_bits": f"K{wl.k_bits}V{wl.v_bits}",
                        "group_size": wl.group_size, "residual": wl.residual_length,
                        "parallelism": f"batch-sharded x{world}", "split_tokens": args.split_tokens,
-                       "num_splits": per_layer[0].num_splits,
+                       "num_splits": fused[0].num_splits,
                        "l2": f"inputs {step_bytes / 1e6:.0f} MB per step > 126 MB L2; layers rotate, no flush",
-                       "timing": "CUDA graph of per-layer launches, CUDA events, max over ranks"},
+                       "timing": "all layers of the step in one launch, CUDA graph, CUDA events, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(wl.name),
-                         "kernel": "kvr::dec::decode_kernel (one layer per launch)",
-                         "bytes_per_launch": lb["total"], "launch_us": launch_us, "peak_source": peak_src,
+                         "kernel": "kvr::dec::decode_kernel, all layers of the step per launch",
+                         "bytes_per_launch": bytes_per_launch, "launch_us": launch_us, "peak_source": peak_src,
                          "frac_note": "of measured" if "measured" in peak_src else "of fallback"},
-            "fused_layers": {"ms_per_step": fused_step_ms, "us_per_step": fused_step_ms * 1e3,
-                             "gbps": step_bytes * world / (fused_step_ms * 1e-3) / 1e9,
-                             "frac": step_bytes / (fused_step_ms * 1e-3) / 1e9 / peak,
-                             "launches_per_step": len(fused), "num_splits": fused[0].num_splits},
-            "e2e": e2e, "cpu_baseline": cpu,
-            "gpu_launches": args.steps * wl.layers,
+            "per_layer": {"ms_per_step": layer_step_ms, "us_per_layer": layer_step_ms * 1e3 / wl.layers,
+                          "gbps": step_bytes * world / (layer_step_ms * 1e-3) / 1e9,
+                          "num_splits": per_layer[0].num_splits,
+                          "timing": "one launch per layer, 28 launches replayed as a CUDA graph"},
+            "e2e": e2e, "e2e_per_layer_calls": e2e_per_layer, "cpu_baseline": cpu,
+            "gpu_launches": args.steps * len(fused),
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_split_sequence(args, wl, world, rank, local):
+    """One batch-1 sequence, its tokens split across the ranks (strong scaling).
+
+    Each rank packs every layer and keeps its 32-token-aligned token shard
+    (kv_reduce_b200.distributed.shard_component); a step is one partial
+    decode launch over all layers of the shard, an NCCL all-gather of the
+    (m, l, o) partials and the LSE merge kernel.  The step time is the max
+    over ranks; `value` counts the whole sequence's bytes once.
+    """
+    import torch.distributed as dist
+
+    import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import distributed as kd
+    from kv_reduce_b200 import workloads
+    from kv_reduce_b200.packed_kv_attention import DecodeLaunch, _geometry, _layer_ptrs
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    a, b = kd.token_shards(wl.seq_len, world, align=wl.group_size)[rank]
+    ks, vs, qs = [], [], []
+    for layer in range(wl.layers):
+        k, v = workloads.make_layer_kv(wl, layer, device=device)
+        pk, pv = kvr.pack_kivi_kv(k, v, k_bits=wl.k_bits, v_bits=wl.v_bits, group_size=wl.group_size,
+                                  residual_length=wl.residual_length)
+        sk, sv = kd.shard_component(pk, pv, a, b)
+        del k, v, pk, pv
+        ks.append(sk)
+        vs.append(sv)
+        qs.append(workloads.make_query(wl, layer, device=device))
+    torch.cuda.synchronize()
+    rows = wl.layers * wl.batch * wl.q_heads
+    dummy = [torch.empty_like(q) for q in qs]
+    geom = _geometry(qs[0], ks[0], vs[0])
+    launch = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
+                          split_tokens=args.split_tokens)
+    out = torch.empty(rows, wl.head_dim, dtype=torch.bfloat16, device=device)
+    dec = kd.SequenceShardDecoder(rows, wl.head_dim, world, device, partial_fn=launch.partial,
+                                  merge_fn=lambda ml, o: kvr.lse_merge(ml, o, out=out))
+
+    def step():
+        dec.step()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(args.steps):
+        step()
+    s1.record()
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    lb = workloads.layer_bytes(wl)
+    step_bytes = lb["total"] * wl.layers
+    if rank == 0:
+        peak, peak_src = measured_peak()
+        value = step_bytes / (ms * 1e-3) / 1e9
+        line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "us_per_step": ms * 1e3,
+                "tokens_per_s": wl.batch / (ms * 1e-3), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "u4 codes; f16/bf16 mma, fp32 accumulate and softmax",
+                "data": "synthetic (seeded N(0,1) K/V/Q, outlier key channels)",
+                "config": {"workload": wl.name, "layers": wl.layers, "global_batch": wl.batch,
+                           "seq_len": wl.seq_len, "parallelism": f"token-split x{world}",
+                           "shard_tokens": b - a, "num_splits": launch.num_splits,
+                           "timing": "eager: partial decode (all layers, one launch) + NCCL all-gather "
+                                     "+ LSE merge per step, CUDA events, max over ranks"},
+                "per_gpu_fraction_of_peak": value / world / peak, "peak_source": peak_src,
+                "gpu_launches": args.steps * 2}
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
@@ -403,6 +512,9 @@ def main():
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
         run_reference(args, wl, world, rank)
+        return
+    if args.split_sequence:
+        run_split_sequence(args, wl, world, rank, local)
         return
     run_ours(args, wl, world, rank, local)
 

@@ -60,7 +60,8 @@ struct Cfg {
   static constexpr int V_OFF = kChunk * RBK;
   static constexpr int M_OFF = V_OFF + kChunk * RBV;
   static constexpr int META = 4 * D;      // scale + offset bf16 for one group
-  static constexpr int STAGE = M_OFF + 2 * META;   // two group slots
+  static constexpr int VM_OFF = M_OFF + 2 * META;  // value scale[32] then offset[32], bf16
+  static constexpr int STAGE = VM_OFF + 2 * kChunk * 2;
   static constexpr int RING = kStages * STAGE;
   // staged query per lane: D/8 fp16x2 words in key-register order (q / f)
   // then the D/8 raw bf16x2 words of its head-dim slice, as uint4 [D/16][32]
@@ -103,6 +104,7 @@ struct Params {
   int tok_begin, tok_end;        // token range processed (begin multiple of 32)
   int num_splits, chunks_per_split, items, groups1;
   int64_t kp_bh, km_bh, kr_bh, vp_bh, vm_bh;
+  int vm_staged;                 // value scale/offset rows 16-byte aligned: copy them with the chunk
   float score_scale_log2;        // log2(e) / sqrt(D)
   int out_f32;                   // 1: fp32 output, 0: bf16
   float* part1;                  // [units][NS][pstride]
@@ -346,6 +348,33 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
       const int n_valid = min(kChunk, t_end - tok0);
       const int n_pref = max(0, min(n_valid, P - tok0));
       const uint32_t st = ring_s + stage * C::STAGE;
+      if (n_pref == kChunk && log2G >= 5) {
+        // Full prefix chunk in one key group (the common case).  Piece k of
+        // this lane sits at row lane/CR + k*32/CR, byte (lane%CR)*16, and its
+        // swizzle term ((row / (8/CR)) % CR) reduces to (lane/8 + 4k) % CR, so
+        // every copy is a per-lane base plus a compile-time offset.
+        const uint8_t* ks = kp + (int64_t)tok0 * C::RBK + 16 * lane;
+        const uint8_t* vs = vp + (int64_t)tok0 * C::RBV + 16 * lane;
+        const uint32_t kd = st + C::K_OFF + (lane / C::CRK) * C::RBK +
+                            16 * ((lane % C::CRK) ^ ((lane >> 3) & (C::CRK - 1)));
+        const uint32_t vd = st + C::V_OFF + (lane / C::CRV) * C::RBV +
+                            16 * ((lane % C::CRV) ^ ((lane >> 3) & (C::CRV - 1)));
+#pragma unroll
+        for (int k = 0; k < C::CRK; ++k)
+          cp_async16(((C::CRK == 8 && (k & 1)) ? (kd ^ 64u) : kd) + 512 * k, ks + 512 * k);
+#pragma unroll
+        for (int k = 0; k < C::CRV; ++k)
+          cp_async16(((C::CRV == 8 && (k & 1)) ? (vd ^ 64u) : vd) + 512 * k, vs + 512 * k);
+        if (lane < D / 4) {   // key scale (lanes < D/8) and offset of the group, slot 0
+          const int which = lane / (D / 8), k16 = lane % (D / 8);
+          cp_async16(st + C::M_OFF + which * 2 * D + 16 * k16,
+                     (which ? kof : ksc) + (int64_t)(tok0 >> log2G) * D + 8 * k16);
+        }
+        if (p.vm_staged && lane < 8)
+          cp_async16(st + C::VM_OFF + (lane >> 2) * 2 * kChunk + 16 * (lane & 3),
+                     ((lane >> 2) ? vof : vsc) + tok0 + 8 * (lane & 3));
+        return;
+      }
       const uint8_t* ksrc = kp + (int64_t)tok0 * C::RBK;
       const uint8_t* vsrc = vp + (int64_t)tok0 * C::RBV;
 #pragma unroll
@@ -361,6 +390,13 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         const int row = pc / C::CRV, c16 = pc % C::CRV;
         if (row < n_valid)
           cp_async16(st + C::V_OFF + row * C::RBV + 16 * (c16 ^ swz<C::CRV>(row)), vsrc + 16 * pc);
+      }
+      if (p.vm_staged && lane < 8) {
+        // 8 pieces: value scale then value offset, 8 tokens each (tokens past
+        // the end of the range stay inside the slab: its length is a multiple of 8)
+        const int k16 = lane & 3;
+        if (8 * k16 < n_valid)
+          cp_async16(st + C::VM_OFF + (lane >> 2) * 2 * kChunk + 16 * k16, ((lane >> 2) ? vof : vsc) + tok0 + 8 * k16);
       }
       if (n_pref > 0) {
         // group slots: 0 <- group of rows 0..15, 1 <- group of rows 16..31 if different
@@ -390,7 +426,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     auto load_vmeta = [&](int c) -> uint32_t {
       const int t = c * kChunk + lane;
       uint32_t s = 0u, z = 0u;
-      if (t < t_end) {
+      if (!p.vm_staged && t < t_end) {
         s = __ldg(vsc + t);
         z = __ldg(vof + t);
       }
@@ -565,8 +601,17 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         // token scale s and centred offset z + 2^(vb-1) s of rows g, g+8
-        const uint32_t w_lo = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g);
-        const uint32_t w_hi = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g + 8);
+        uint32_t w_lo, w_hi;
+        if (p.vm_staged) {
+          // rows past the end of a partial chunk were not copied: use zero
+          const uint16_t* vm = reinterpret_cast<const uint16_t*>(st + C::VM_OFF);
+          const int r = 16 * mt + g;
+          w_lo = r < n_valid ? ((uint32_t)vm[r] | ((uint32_t)vm[kChunk + r] << 16)) : 0u;
+          w_hi = r + 8 < n_valid ? ((uint32_t)vm[r + 8] | ((uint32_t)vm[kChunk + r + 8] << 16)) : 0u;
+        } else {
+          w_lo = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g);
+          w_hi = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g + 8);
+        }
         const float s_lo = bf16lo(w_lo), s_hi = bf16lo(w_hi);
         const float z_lo = fmaf(s_lo, (float)(1 << (VB - 1)), bf16hi(w_lo));
         const float z_hi = fmaf(s_hi, (float)(1 << (VB - 1)), bf16hi(w_hi));
@@ -913,6 +958,10 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   p.kr_bh = a->key_residual_bh_stride;
   p.vp_bh = a->value_payload_bh_stride;
   p.vm_bh = a->value_meta_bh_stride;
+  bool staged = a->value_meta_bh_stride % 8 == 0;
+  for (int l = 0; l < a->n_layers; ++l)
+    staged = staged && aligned16(a->layers[l].value_scale) && aligned16(a->layers[l].value_offset);
+  p.vm_staged = staged ? 1 : 0;
   p.score_scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)a->head_dim));
   p.out_f32 = a->out_dtype == 1;
   const int64_t units = (int64_t)a->n_layers * a->batch * a->kv_heads;

@@ -120,9 +120,14 @@ class SequenceShardDecoder:
 
         self.partial_fn(self.ml, self.o)
         if self.world > 1:
-            # list form: works on NCCL and gloo alike; the views land in place
-            dist.all_gather(list(self.ml_all.unbind(0)), self.ml, group=self.group)
-            dist.all_gather(list(self.o_all.unbind(0)), self.o, group=self.group)
+            if dist.get_backend(self.group) == "nccl":
+                # one NCCL all-gather per buffer straight into the stacked output
+                dist.all_gather_into_tensor(self.ml_all, self.ml, group=self.group)
+                dist.all_gather_into_tensor(self.o_all, self.o, group=self.group)
+            else:
+                # gloo has no stacked form: gather into views of the same buffers
+                dist.all_gather(list(self.ml_all.unbind(0)), self.ml, group=self.group)
+                dist.all_gather(list(self.o_all.unbind(0)), self.o, group=self.group)
         else:
             self.ml_all[0].copy_(self.ml)
             self.o_all[0].copy_(self.o)

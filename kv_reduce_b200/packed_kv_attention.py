@@ -131,17 +131,43 @@ def _layer_ptrs(query: torch.Tensor, out: torch.Tensor, k: PackedKVComponent,
 
 
 # Split-merge counters: zero on entry, left zero by every completed launch,
-# so one array per (device, stream) serves all launches on that stream.
+# so one array per (device, stream) serves all launches on that stream.  The
+# split-partial workspace is scratch that stream-ordered launches can share
+# the same way.  A launch object keeps references to the buffers it was
+# built with, so growing a cached buffer never frees memory still in use.
 _COUNTERS: Dict[Tuple[int, int], torch.Tensor] = {}
+_WORKSPACE: Dict[Tuple[int, int], torch.Tensor] = {}
+_PLANS: Dict[tuple, Tuple[int, int, int]] = {}
+_SMS: Dict[int, int] = {}
+
+
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
 
 
 def _counters(device: torch.device, stream: int, n: int) -> torch.Tensor:
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+    key = (_dev_index(device), stream)
     buf = _COUNTERS.get(key)
     if buf is None or buf.numel() < n:
         buf = torch.zeros(max(n, 1024), dtype=torch.int32, device=device)
         _COUNTERS[key] = buf
     return buf
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (_dev_index(device), stream)
+    buf = _WORKSPACE.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _WORKSPACE[key] = buf
+    return buf
+
+
+def _num_sms(device: torch.device) -> int:
+    idx = _dev_index(device)
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
 
 
 class DecodeLaunch:
@@ -173,14 +199,20 @@ class DecodeLaunch:
         a.value_meta_bh_stride = geom.vm_bh
         a.out_dtype = 1 if out_fp32 else 0
         a.split_tokens = int(split_tokens)
-        a.num_sms = torch.cuda.get_device_properties(device).multi_processor_count
-        ns, wsb, ncnt = ctypes.c_int(0), ctypes.c_size_t(0), ctypes.c_size_t(0)
-        _lib.check("kvr_decode_plan", _lib.load().kvr_decode_plan(a, ctypes.byref(ns), ctypes.byref(wsb),
-                                                                 ctypes.byref(ncnt)))
-        self.num_splits = ns.value
-        self.workspace = torch.empty(max(int(wsb.value), 16), dtype=torch.uint8, device=device)
-        self.counters = _counters(device, self.stream, int(ncnt.value))
-        a.workspace, a.workspace_bytes = self.workspace.data_ptr(), int(wsb.value)
+        a.num_sms = _num_sms(device)
+        key = (geom, len(layers), a.split_tokens, _dev_index(device), int(token_begin),
+               geom.seq_len if token_end is None else int(token_end))
+        plan = _PLANS.get(key)
+        if plan is None:
+            ns, wsb, ncnt = ctypes.c_int(0), ctypes.c_size_t(0), ctypes.c_size_t(0)
+            _lib.check("kvr_decode_plan", _lib.load().kvr_decode_plan(a, ctypes.byref(ns), ctypes.byref(wsb),
+                                                                     ctypes.byref(ncnt)))
+            plan = (ns.value, int(wsb.value), int(ncnt.value))
+            _PLANS[key] = plan
+        self.num_splits, ws_bytes, n_counters = plan
+        self.workspace = _workspace(device, self.stream, ws_bytes)
+        self.counters = _counters(device, self.stream, n_counters)
+        a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
         a.counters = self.counters.data_ptr()
         self.args = a
         self.token_begin = int(token_begin)
