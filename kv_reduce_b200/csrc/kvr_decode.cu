@@ -11,17 +11,20 @@
 //           XOR-swizzled so the tensor-core operand reads are conflict free)
 //   QK^T  = mma.sync m16n8k16, M = 16 tokens, N = 8 query heads of the GQA
 //           group (each packed byte is read once for all heads), K = head dim.
-//           Key codes become exact fp16 integers in registers with the
-//           0x6400 magic-exponent method (code | 0x6400 is 1024 + code); the
-//           per-channel key scale is folded into the query,
-//           q~ = q * s_g * log2e/sqrt(D), carried as an fp16 hi + lo pair so
-//           the logits keep ~22 bits; the zero point enters as a per-group
-//           bias q . z_g in fp32.
+//           Key codes become exact fp16 subnormals in registers with one AND
+//           (code bits in the mantissa of a zero exponent: c * f * 2^-24);
+//           the per-channel key scale is folded into the query,
+//           q~ = (q / f) * s_g (f = the code's bit-position factor), carried
+//           as an exact fp16 hi + lo pair (TwoProduct); the zero point enters
+//           as a per-group bias q . z_g from a bf16 mma; scores are scaled by
+//           2^24 * log2e / sqrt(D) after the mma.
 //   softmax = fp32 online softmax in log2 units with warp-shuffle reductions.
 //   P V    = mma.sync with M = head dim, N = heads, K = 16 tokens: P moves
 //           from accumulator to operand layout with movmatrix.trans, value
-//           codes arrive token-paired through ldmatrix.trans and are centred
-//           (n - 2^(b-1)), the per-token value scale is folded into P
+//           codes arrive token-paired through ldmatrix.trans, become fp16 by
+//           the 0x6400 magic-exponent method (code | 0x6400 is 1024 + code)
+//           and are centred (n - 2^(b-1)) by the same subtraction, the
+//           per-token value scale is folded into P
 //           (P~ = p * s_t) and the zero point is accumulated as
 //           sum p * (z_t + 2^(b-1) s_t) in fp32.
 //   BF16 residual window = same pass, bf16 mma of raw keys against the raw
@@ -147,6 +150,20 @@ __device__ __forceinline__ uint32_t codes_to_h2(uint32_t w, int j) {
   return hsub2_u32(lop_and_or(x, code_mask<B>(j), kMagic), sub_const<B>(j, CENTRED));
 }
 
+// Key code slot j of both halves as exact fp16x2 subnormals
+// {c_lo * f * 2^-24, c_hi * f * 2^-24}: the masked code bits sit in the
+// mantissa of a zero exponent field (f = 2^(B * (j % (8/B))) <= 64, so the
+// value stays below 2^-14).  The tensor cores take fp16 subnormal operands
+// exactly; the 2^-24 is folded into the score scale, so no subtraction of a
+// magic-number bias is needed.
+template <int B>
+__device__ __forceinline__ uint32_t key_codes_h2(uint32_t w, int j) {
+  const uint32_t x = (j / (8 / B)) ? (w >> 8) : w;
+  return x & code_mask<B>(j);
+}
+constexpr float kKeyUnscale = 16777216.f;          // 2^24
+constexpr float kKeyScale = 1.f / 16777216.f;      // 2^-24
+
 // Per-chunk state of one warp's query transform for a key group.
 template <int D>
 struct GroupQ {
@@ -267,14 +284,14 @@ __device__ __forceinline__ void qk_chunk(float (&h0)[4], float (&l0)[4], float (
       two_prod_h2(qw[r - base], pack_half2(s0, s1), bh[k], bl[k]);
     }
     const int r0 = 2 * js, r1 = 2 * js + 1;
-    const uint32_t a0 = codes_to_h2<KB, false>(kw[0][r0 / RPW], r0 % RPW);
-    const uint32_t a1 = codes_to_h2<KB, false>(kw[1][r0 / RPW], r0 % RPW);
-    const uint32_t a2 = codes_to_h2<KB, false>(kw[0][r1 / RPW], r1 % RPW);
-    const uint32_t a3 = codes_to_h2<KB, false>(kw[1][r1 / RPW], r1 % RPW);
-    const uint32_t b0 = codes_to_h2<KB, false>(kw[2][r0 / RPW], r0 % RPW);
-    const uint32_t b1 = codes_to_h2<KB, false>(kw[3][r0 / RPW], r0 % RPW);
-    const uint32_t b2 = codes_to_h2<KB, false>(kw[2][r1 / RPW], r1 % RPW);
-    const uint32_t b3 = codes_to_h2<KB, false>(kw[3][r1 / RPW], r1 % RPW);
+    const uint32_t a0 = key_codes_h2<KB>(kw[0][r0 / RPW], r0 % RPW);
+    const uint32_t a1 = key_codes_h2<KB>(kw[1][r0 / RPW], r0 % RPW);
+    const uint32_t a2 = key_codes_h2<KB>(kw[0][r1 / RPW], r1 % RPW);
+    const uint32_t a3 = key_codes_h2<KB>(kw[1][r1 / RPW], r1 % RPW);
+    const uint32_t b0 = key_codes_h2<KB>(kw[2][r0 / RPW], r0 % RPW);
+    const uint32_t b1 = key_codes_h2<KB>(kw[3][r0 / RPW], r0 % RPW);
+    const uint32_t b2 = key_codes_h2<KB>(kw[2][r1 / RPW], r1 % RPW);
+    const uint32_t b3 = key_codes_h2<KB>(kw[3][r1 / RPW], r1 % RPW);
     mma_f16(h0, a0, a1, a2, a3, bh[0], bh[1]);
     mma_f16(h1, b0, b1, b2, b3, bh[0], bh[1]);
     mma_f16(l0, a0, a1, a2, a3, bl[0], bl[1]);
@@ -290,10 +307,10 @@ __device__ __forceinline__ void qk_prefix(float (&hi)[4], float (&lo)[4], const 
 #pragma unroll
   for (int js = 0; js < D / 16; ++js) {
     const int r0 = 2 * js, r1 = 2 * js + 1;
-    const uint32_t a0 = codes_to_h2<KB, false>(kw0[r0 / RPW], r0 % RPW);
-    const uint32_t a1 = codes_to_h2<KB, false>(kw1[r0 / RPW], r0 % RPW);
-    const uint32_t a2 = codes_to_h2<KB, false>(kw0[r1 / RPW], r1 % RPW);
-    const uint32_t a3 = codes_to_h2<KB, false>(kw1[r1 / RPW], r1 % RPW);
+    const uint32_t a0 = key_codes_h2<KB>(kw0[r0 / RPW], r0 % RPW);
+    const uint32_t a1 = key_codes_h2<KB>(kw1[r0 / RPW], r0 % RPW);
+    const uint32_t a2 = key_codes_h2<KB>(kw0[r1 / RPW], r1 % RPW);
+    const uint32_t a3 = key_codes_h2<KB>(kw1[r1 / RPW], r1 % RPW);
     mma_f16(hi, a0, a1, a2, a3, gq.hi[r0], gq.hi[r1]);
     mma_f16(lo, a0, a1, a2, a3, gq.lo[r0], gq.lo[r1]);
   }
@@ -316,6 +333,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
   const uint32_t ring_s = smem_u32(ring);
   uint4* qs = reinterpret_cast<uint4*>(smem + C::QS_OFF);
   const float cs = p.score_scale_log2;
+  const float cs_k = cs * kKeyUnscale;   // quantized-key scores carry the codes' 2^-24
 
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
     const int sp = item % NS;
@@ -392,10 +410,10 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
           cp_async16(st + C::V_OFF + row * C::RBV + 16 * (c16 ^ swz<C::CRV>(row)), vsrc + 16 * pc);
       }
       if (p.vm_staged && lane < 8) {
-        // 8 pieces: value scale then value offset, 8 tokens each (tokens past
-        // the end of the range stay inside the slab: its length is a multiple of 8)
+        // 8 pieces: value scale then value offset, 8 tokens each; only whole
+        // pieces inside the chunk (a ragged tail is read directly when used)
         const int k16 = lane & 3;
-        if (8 * k16 < n_valid)
+        if (8 * k16 + 8 <= n_valid)
           cp_async16(st + C::VM_OFF + (lane >> 2) * 2 * kChunk + 16 * k16, ((lane >> 2) ? vof : vsc) + tok0 + 8 * k16);
       }
       if (n_pref > 0) {
@@ -509,13 +527,15 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         uint32_t kw[4][C::NWK];
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) load_key_row<D, KB>(kw[rr], st + C::K_OFF, g + 8 * rr, t4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) bf[k] *= kKeyScale;
         float h0[4] = {bf[0], bf[1], bf[2], bf[3]}, l0[4] = {0.f, 0.f, 0.f, 0.f};
         float h1[4] = {bf[0], bf[1], bf[2], bf[3]}, l1[4] = {0.f, 0.f, 0.f, 0.f};
         qk_chunk<D, KB>(h0, l0, h1, l1, kw, qs, meta0, lane, dbase);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          sc[0][k] = (h0[k] + l0[k]) * cs;
-          sc[1][k] = (h1[k] + l1[k]) * cs;
+          sc[0][k] = (h0[k] + l0[k]) * cs_k;
+          sc[1][k] = (h1[k] + l1[k]) * cs_k;
         }
       } else {
 #pragma unroll
@@ -531,10 +551,11 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
             uint32_t kw0[C::NWK], kw1[C::NWK];
             load_key_row<D, KB>(kw0, st + C::K_OFF, 16 * mt + g, t4);
             load_key_row<D, KB>(kw1, st + C::K_OFF, 16 * mt + g + 8, t4);
-            float hi[4] = {gq.bias[0], gq.bias[1], gq.bias[0], gq.bias[1]}, lo[4] = {0.f, 0.f, 0.f, 0.f};
+            const float b0 = gq.bias[0] * kKeyScale, b1 = gq.bias[1] * kKeyScale;
+            float hi[4] = {b0, b1, b0, b1}, lo[4] = {0.f, 0.f, 0.f, 0.f};
             qk_prefix<D, KB>(hi, lo, kw0, kw1, gq);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) sc[mt][k] = (hi[k] + lo[k]) * cs;
+            for (int k = 0; k < 4; ++k) sc[mt][k] = (hi[k] + lo[k]) * cs_k;
           } else {
             // BF16 residual window: raw keys x raw query, bf16 mma.
             uint32_t kr[2][D / 8];
@@ -603,11 +624,18 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         // token scale s and centred offset z + 2^(vb-1) s of rows g, g+8
         uint32_t w_lo, w_hi;
         if (p.vm_staged) {
-          // rows past the end of a partial chunk were not copied: use zero
+          // rows [0, n_vm) were copied; the ragged tail [n_vm, n_valid) is
+          // read from global memory; rows past the end contribute zero
           const uint16_t* vm = reinterpret_cast<const uint16_t*>(st + C::VM_OFF);
+          const int n_vm = n_valid & ~7;
+          auto vmeta = [&](int r) -> uint32_t {
+            if (r < n_vm) return (uint32_t)vm[r] | ((uint32_t)vm[kChunk + r] << 16);
+            if (r < n_valid) return (uint32_t)__ldg(vsc + tok0 + r) | ((uint32_t)__ldg(vof + tok0 + r) << 16);
+            return 0u;
+          };
           const int r = 16 * mt + g;
-          w_lo = r < n_valid ? ((uint32_t)vm[r] | ((uint32_t)vm[kChunk + r] << 16)) : 0u;
-          w_hi = r + 8 < n_valid ? ((uint32_t)vm[r + 8] | ((uint32_t)vm[kChunk + r + 8] << 16)) : 0u;
+          w_lo = vmeta(r);
+          w_hi = vmeta(r + 8);
         } else {
           w_lo = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g);
           w_hi = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g + 8);

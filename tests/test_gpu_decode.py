@@ -206,3 +206,31 @@ def test_api_errors(kvr):
     k3, v3 = kvr.pack_kivi_kv(k, v, k_bits=3, v_bits=4, group_size=32, residual_length=0)
     with pytest.raises(ValueError):
         kvr.packed_kv_decode_attention(q, k3, v3)
+
+
+def test_value_metadata_in_padded_rows(kvr):
+    """Value scale/offset rows padded to a multiple of 8 tokens (a capacity
+    buffer) with a ragged sequence end: whole 8-token pieces travel with the
+    chunk's copies, the tail is read directly, and the NaN padding past the
+    sequence must not reach the output."""
+    import dataclasses
+
+    S, cap = 1001, 1008
+    k, v, q = make((2, 2, S, 128), 12, 4, 4, 32, 128, seed=17)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+
+    def padded(t):
+        shape = list(t.shape)
+        shape[2] = cap
+        buf = torch.full(shape, float("nan"), dtype=t.dtype, device=t.device)
+        buf[:, :, :S] = t
+        return buf[:, :, :S]
+
+    pv_cap = dataclasses.replace(pv, scale=padded(pv.scale), offset=padded(pv.offset))
+    ref = oracle_out(k, v, q, 4, 4, 32, 128)
+    for split in (0, 64):
+        dense = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=split, out_dtype=F32)
+        strided = kvr.packed_kv_decode_attention(q, pk, pv_cap, split_tokens=split, out_dtype=F32)
+        check(strided, ref, f"padded value metadata split={split}")
+        assert torch.equal(dense, strided)
+
