@@ -20,6 +20,7 @@ from .packed_kv_cache import (  # noqa: F401
 )
 from .packed_kv_attention import (  # noqa: F401
     DecodeLaunch,
+    PackedDecoder,
     lse_merge,
     packed_kv_decode_attention,
     packed_kv_decode_attention_layers,

@@ -121,12 +121,23 @@ def _geometry(query: torch.Tensor, k: PackedKVComponent, v: PackedKVComponent) -
                          kb, vb, kp_bh, km_bh, kr_bh, vp_bh, vm_bh)
 
 
-def _layer_ptrs(query: torch.Tensor, out: torch.Tensor, k: PackedKVComponent,
+def _check_device(dev_index: int, k: PackedKVComponent, v: PackedKVComponent) -> None:
+    """Every cache tensor must live on the query's GPU (the kernel reads them
+    through device pointers; a host tensor's address would be read as one)."""
+    for t in (k.payload, k.scale, k.offset, k.residual, v.payload, v.scale, v.offset):
+        if t is not None and (not t.is_cuda or t.get_device() != dev_index):
+            raise ValueError("Packed K/V tensors must be on the query's CUDA device.")
+
+
+def _layer_ptrs(query: torch.Tensor | None, out: torch.Tensor | None, k: PackedKVComponent,
                 v: PackedKVComponent) -> _lib.LayerPtrs:
+    """Device pointers of one layer; query/out may be filled in later (None)."""
+    _check_device(query.get_device() if query is not None else k.payload.get_device(), k, v)
     res = k.residual if (k.residual is not None and k.residual.numel()) else None
     return _lib.LayerPtrs(
         _lib.ptr(k.payload), _lib.ptr(k.scale), _lib.ptr(k.offset), _lib.ptr(res),
-        _lib.ptr(v.payload), _lib.ptr(v.scale), _lib.ptr(v.offset), query.data_ptr(), out.data_ptr(),
+        _lib.ptr(v.payload), _lib.ptr(v.scale), _lib.ptr(v.offset),
+        query.data_ptr() if query is not None else None, out.data_ptr() if out is not None else None,
     )
 
 
@@ -188,6 +199,7 @@ class DecodeLaunch:
         self.device = device
         self.stream = _lib.stream_ptr(device) if stream is None else stream
         self._layers = (_lib.LayerPtrs * len(layers))(*layers)
+        self.layers = self._layers   # per-layer pointers; PackedDecoder rewrites query/out in place
         a = _lib.DecodeArgs()
         a.layers = ctypes.cast(self._layers, ctypes.POINTER(_lib.LayerPtrs))
         a.n_layers = len(layers)
@@ -267,31 +279,128 @@ def packed_kv_decode_attention_layers(
     packed_values: Sequence[PackedKVComponent],
     *,
     split_tokens: int = 0,
+    out: torch.Tensor | None = None,
 ) -> List[torch.Tensor]:
     """Decode attention for several layers of equal geometry in one launch.
 
     Each layer is independent (its own query, cache and output); the result
-    equals calling packed_kv_decode_attention per layer.
+    equals calling packed_kv_decode_attention per layer.  ``out`` (optional,
+    [L, *query.shape], the query dtype or fp32) receives all layers' outputs;
+    the returned list holds its per-layer views.
     """
-    if not (len(queries) == len(packed_keys) == len(packed_values)) or not queries:
+    n = len(queries)
+    if not (n == len(packed_keys) == len(packed_values)) or not n:
         raise ValueError("queries, packed_keys and packed_values must be non-empty and equally long.")
-    outs, ptrs, geom = [], [], None
-    for q, k, v in zip(queries, packed_keys, packed_values):
-        _validate(q, k, v, 32)
-        q = q.contiguous()
-        g = _geometry(q, k, v)
-        if geom is None:
-            geom = g
-        elif g != geom:
-            raise ValueError("All layers of one launch must share geometry and strides.")
-        o = torch.empty_like(q)
-        outs.append(o)
-        ptrs.append(_layer_ptrs(q, o, k, v))
-    out_all: List[torch.Tensor] = []
-    for start in range(0, len(ptrs), _lib.KVR_MAX_LAYERS):
-        DecodeLaunch(geom, ptrs[start:start + _lib.KVR_MAX_LAYERS], queries[0].device, split_tokens=split_tokens)()
-    out_all.extend(outs)
-    return out_all
+    q0 = queries[0]
+    _validate(q0, packed_keys[0], packed_values[0], 32)
+    geom = _geometry(q0, packed_keys[0], packed_values[0])
+    if out is None:
+        out = torch.empty((n,) + tuple(q0.shape), dtype=q0.dtype, device=q0.device)
+    elif (tuple(out.shape) != (n,) + tuple(q0.shape) or out.dtype not in (q0.dtype, torch.float32)
+          or out.device != q0.device or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous [layers, *query.shape] tensor of the query dtype or fp32.")
+    outs = list(out.unbind(0))
+    ptrs = []
+    for i, (q, k, v) in enumerate(zip(queries, packed_keys, packed_values)):
+        if i:
+            _validate(q, k, v, 32)
+            if _geometry(q, k, v) != geom:
+                raise ValueError("All layers of one launch must share geometry and strides.")
+        ptrs.append(_layer_ptrs(q.contiguous(), outs[i], k, v))
+    for start in range(0, n, _lib.KVR_MAX_LAYERS):
+        DecodeLaunch(geom, ptrs[start:start + _lib.KVR_MAX_LAYERS], q0.device, split_tokens=split_tokens,
+                     out_fp32=out.dtype == torch.float32)()
+    return outs
+
+
+class PackedDecoder:
+    """Plan once, run every decode step: attention for all layers of a cache.
+
+    Construction validates every layer (the same preconditions and messages
+    as packed_kv_decode_attention), resolves the cache pointers and the split
+    plan, and builds the launch argument blocks.  A call then takes the
+    step's stacked queries [L, B, HQ, 1, D] (bf16) and writes all layers'
+    outputs with one library call per 32 layers; the cache pointers are
+    not re-derived, so the per-step host cost does not grow with the number
+    of layers.  The cache tensors must stay alive and in place (a streaming
+    cache that appends or reallocates needs a new decoder).  Launches go to
+    the CUDA stream current at the first call.
+    """
+
+    def __init__(self, packed_keys: Sequence[PackedKVComponent], packed_values: Sequence[PackedKVComponent],
+                 *, q_heads: int, split_tokens: int = 0, out_dtype: torch.dtype = torch.bfloat16) -> None:
+        n = len(packed_keys)
+        if n == 0 or n != len(packed_values):
+            raise ValueError("packed_keys and packed_values must be non-empty and equally long.")
+        if out_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("out_dtype must be torch.bfloat16 or torch.float32.")
+        k0 = packed_keys[0]
+        if k0.payload is None or not k0.payload.is_cuda:
+            raise ValueError("Packed attention requires CUDA cache tensors.")
+        device = k0.payload.device
+        batch, _, _, head_dim = (int(x) for x in k0.shape)
+        # a query of the step's shape: the reference's checks take one
+        probe = torch.empty(batch, int(q_heads), 1, head_dim, dtype=torch.bfloat16, device=device)
+        geom, layers = None, []
+        dev_index = probe.get_device()
+        for k, v in zip(packed_keys, packed_values):
+            _validate(probe, k, v, 32)
+            _check_device(dev_index, k, v)
+            g = _geometry(probe, k, v)
+            if geom is None:
+                geom = g
+            elif g != geom:
+                raise ValueError("All layers must share geometry and strides.")
+            layers.append(_layer_ptrs(None, None, k, v))
+        self.geom, self.device, self.n_layers = geom, device, n
+        self.q_shape = (n,) + tuple(probe.shape)
+        self.out_dtype = out_dtype
+        self.split_tokens = int(split_tokens)
+        self._keep = (list(packed_keys), list(packed_values))
+        self._layers = layers
+        self._launches: List[DecodeLaunch] = []   # built at the first call, with real query/out pointers
+        self._q_step = head_dim * int(q_heads) * batch * 2
+        self._o_step = head_dim * int(q_heads) * batch * (4 if out_dtype == torch.float32 else 2)
+        self._bases = (0, 0)
+
+    @property
+    def num_splits(self) -> int:
+        if not self._launches:
+            raise RuntimeError("the split plan is made at the first call")
+        return self._launches[0].num_splits
+
+    def _build(self, qb: int, ob: int) -> None:
+        for i, layer in enumerate(self._layers):
+            layer.query = qb + i * self._q_step
+            layer.out = ob + i * self._o_step
+        self._launches = [DecodeLaunch(self.geom, self._layers[s:s + _lib.KVR_MAX_LAYERS], self.device,
+                                       split_tokens=self.split_tokens, out_fp32=self.out_dtype == torch.float32)
+                          for s in range(0, self.n_layers, _lib.KVR_MAX_LAYERS)]
+
+    def __call__(self, queries: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if (tuple(queries.shape) != self.q_shape or queries.dtype != torch.bfloat16 or queries.device != self.device
+                or not queries.is_contiguous()):
+            raise ValueError(f"queries must be a contiguous bf16 tensor of shape {self.q_shape} on {self.device}.")
+        if out is None:
+            out = torch.empty(self.q_shape, dtype=self.out_dtype, device=self.device)
+        elif (tuple(out.shape) != self.q_shape or out.dtype != self.out_dtype or out.device != self.device
+              or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous {self.out_dtype} tensor of shape {self.q_shape}.")
+        bases = (queries.data_ptr(), out.data_ptr())
+        if not self._launches:
+            self._build(*bases)
+            self._bases = bases
+        elif bases != self._bases:
+            qb, ob = bases
+            for li, launch in enumerate(self._launches):
+                for j in range(launch.args.n_layers):
+                    layer = li * _lib.KVR_MAX_LAYERS + j
+                    launch.layers[j].query = qb + layer * self._q_step
+                    launch.layers[j].out = ob + layer * self._o_step
+            self._bases = bases
+        for launch in self._launches:
+            launch()
+        return out
 
 
 def lse_merge(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -234,3 +234,51 @@ def test_value_metadata_in_padded_rows(kvr):
         check(strided, ref, f"padded value metadata split={split}")
         assert torch.equal(dense, strided)
 
+
+
+def test_packed_decoder_equals_per_layer_calls(kvr):
+    """PackedDecoder (planned once, stacked queries) == packed_kv_decode_attention
+    per layer, bit for bit; moving the query/output buffers re-points the launch."""
+    from kv_reduce_b200 import workloads
+
+    wl = workloads.CONFIGS["2"].scaled(seq_len=2100, layers=35)   # > 32 layers: two launches
+    ks, vs, qs = [], [], []
+    for layer in range(wl.layers):
+        k, v = workloads.make_layer_kv(wl, layer)
+        pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+        ks.append(pk)
+        vs.append(pv)
+        qs.append(workloads.make_query(wl, layer))
+    # a fixed split makes the merge order, hence the rounding, independent of
+    # how many layers share a launch (the default plan depends on it)
+    dec = kvr.PackedDecoder(ks, vs, q_heads=wl.q_heads, split_tokens=512)
+    q_all = torch.stack(qs)
+    out = dec(q_all)
+    for i in range(wl.layers):
+        assert torch.equal(out[i], kvr.packed_kv_decode_attention(qs[i], ks[i], vs[i], split_tokens=512))
+    q_moved = q_all.clone()
+    out2 = torch.empty_like(out)
+    assert dec(q_moved, out=out2) is out2
+    assert torch.equal(out2, out)
+    outs = kvr.packed_kv_decode_attention_layers(qs, ks, vs, split_tokens=512, out=torch.empty_like(out))
+    for i in range(wl.layers):
+        assert torch.equal(outs[i], out[i])
+    dec32 = kvr.PackedDecoder(ks[:3], vs[:3], q_heads=wl.q_heads, out_dtype=F32)
+    ref = oracle_out(*workloads.make_layer_kv(wl, 1), qs[1], 4, 4, 32, 128)
+    check(dec32(q_all[:3])[1], ref, "decoder fp32")
+    with pytest.raises(ValueError):
+        dec(q_all[:, :, :6].contiguous())
+    with pytest.raises(ValueError):
+        dec(q_all.float())
+
+
+def test_cache_on_another_device_is_rejected(kvr):
+    k, v, q = make((1, 2, 256, 128), 12, 4, 4, 32, 0, seed=2)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=0)
+    import dataclasses
+
+    cpu_v = dataclasses.replace(pv, payload=pv.payload.cpu())
+    with pytest.raises(ValueError):
+        kvr.packed_kv_decode_attention(q, pk, cpu_v)
+    with pytest.raises(ValueError):
+        kvr.PackedDecoder([pk], [cpu_v], q_heads=12)
