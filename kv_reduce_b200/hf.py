@@ -10,6 +10,9 @@ Mirrors kv_reduce/experiments/packed_review.py:17-80:
   Its layers are the preallocated streaming layers of
   ``kv_reduce_b200.streaming``, so a decode step appends one token in place
   instead of the reference's ``torch.cat`` of the whole payload.
+* ``PackedDraftCache.empty(num_layers, residual)`` packs each layer during
+  the prompt forward itself (streaming prefill): the full BF16 cache the
+  reference builds first and packs afterwards never exists.
 * ``install(model)`` patches every decoder layer's attention (:65-80): with
   a ``PackedDraftCache`` and a one-token step, it projects q/k/v, applies the
   rotary embedding, appends k/v to the packed layer and runs the fused
@@ -29,19 +32,27 @@ from transformers.cache_utils import DynamicCache, DynamicLayer
 from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
 
 from .packed_kv_attention import packed_kv_decode_attention
-from .streaming import PackedLayer
+from .streaming import PackedKVCacheLayer, PackedLayer
 
 
 class PackedDraftLayer(DynamicLayer):
-    """A transformers cache layer over one streaming packed layer."""
+    """A transformers cache layer over one streaming packed layer.
 
-    def __init__(self, packed: PackedLayer) -> None:
+    Built over an already packed layer, or empty: then the prompt forward's
+    ``update`` packs the layer's K/V as soon as they are produced (streaming
+    prefill) and passes the BF16 tensors on to that layer's attention only,
+    so the model never holds a BF16 copy of more than one layer's cache.
+    """
+
+    def __init__(self, packed: PackedKVCacheLayer | None = None, *, residual: int = 128,
+                 spare_capacity: int = 2048, **kw) -> None:
         super().__init__()
         self.packed = packed
+        self._residual, self._spare, self._kw = int(residual), int(spare_capacity), kw
         self.is_initialized = True
 
     def get_seq_length(self) -> int:
-        return self.packed.get_seq_length()
+        return 0 if self.packed is None else self.packed.get_seq_length()
 
     def get_mask_sizes(self, query_length: int) -> Tuple[int, int]:
         return self.get_seq_length() + int(query_length), 0
@@ -52,6 +63,14 @@ class PackedDraftLayer(DynamicLayer):
         self.packed.crop(n + max_length if max_length < 0 else min(max_length, n))
 
     def update(self, key_states, value_states, *args, **kwargs):
+        if self.get_seq_length() == 0:
+            # streaming prefill: pack this layer now (pack_kivi_kv semantics)
+            B, H, S, D = (int(x) for x in key_states.shape)
+            if self.packed is None:
+                self.packed = PackedKVCacheLayer(B, H, D, residual_length=self._residual,
+                                                 capacity=S + self._spare, device=key_states.device, **self._kw)
+            self.packed.prefill(key_states, value_states)
+            return key_states, value_states
         raise RuntimeError("a packed draft cache is extended by the installed attention hook, one token per step "
                            "(call kv_reduce_b200.hf.install(model) first)")
 
@@ -70,12 +89,23 @@ class PackedDraftCache(DynamicCache):
         super().__init__()
         self.layers = [PackedDraftLayer(PackedLayer(k, v, residual, **kw)) for k, v in _legacy_pairs(cache)]
 
+    @classmethod
+    def empty(cls, num_layers: int, residual: int, *, spare_capacity: int = 2048, **kw) -> "PackedDraftCache":
+        """A cache to run the prompt forward into: each layer is packed as the
+        forward produces it (streaming prefill), then decoded through the hook.
+        ``kw`` are PackedKVCacheLayer options (k_bits, v_bits, group_size)."""
+        self = cls([], residual)
+        self.layers = [PackedDraftLayer(None, residual=residual, spare_capacity=spare_capacity, **kw)
+                       for _ in range(int(num_layers))]
+        return self
+
     def commit(self) -> None:
         for layer in self.layers:
-            layer.packed.commit()
+            if layer.packed is not None:
+                layer.packed.commit()
 
     def breakdown(self) -> Dict[str, int]:
-        parts = [layer.packed.breakdown() for layer in self.layers]
+        parts = [layer.packed.breakdown() for layer in self.layers if layer.packed is not None]
         return {key: sum(p[key] for p in parts) for key in parts[0]}
 
 
@@ -90,7 +120,10 @@ def install(model, *, split_tokens: int = 0) -> None:
 
         def forward(self, hidden_states, position_embeddings, attention_mask, past_key_values=None,
                     _original=original, **kwargs):
-            if not isinstance(past_key_values, PackedDraftCache):
+            if (not isinstance(past_key_values, PackedDraftCache)
+                    or past_key_values.layers[self.layer_idx].get_seq_length() == 0):
+                # other caches, and the prompt forward of an empty packed cache
+                # (its update() packs the layer: streaming prefill)
                 return _original(hidden_states, position_embeddings, attention_mask, past_key_values, **kwargs)
             if hidden_states.shape[1] != 1:
                 raise ValueError("the packed draft cache decodes one token per step")

@@ -1,7 +1,8 @@
 """Draft-model integration (kv_reduce/experiments/packed_review.py:17-80) on a
 small random-initialised Qwen2 model: the installed attention hook against
-SDPA over the dequantized packed cache, and a 40-step greedy decode with
-commits against the same model on an unquantized cache."""
+SDPA over the dequantized packed cache, a 40-step greedy decode with commits
+against the same model on an unquantized cache, and streaming prefill (each
+layer packed inside the prompt forward) against packing after the fact."""
 import pytest
 import torch
 
@@ -94,3 +95,40 @@ def test_hook_leaves_other_caches_alone(built_lib):
     packed = hf.PackedDraftCache(model(ids, use_cache=True).past_key_values, residual=0)
     with pytest.raises(ValueError):
         model(ids[:, :2], past_key_values=packed, use_cache=True)
+
+
+@torch.inference_mode()
+def test_streaming_prefill_packs_each_layer_bit_exact(built_lib):
+    """An empty PackedDraftCache packs each layer inside the prompt forward:
+    the prompt logits are the BF16 model's, the packed layers equal
+    pack_kivi_kv of the BF16 cache bit for bit, and decoding continues
+    through the hook exactly as from a cache packed after the fact."""
+    import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import hf
+
+    model = tiny_qwen2(seed=7)
+    prompt = torch.randint(0, 512, (1, 777), device="cuda", generator=torch.Generator("cuda").manual_seed(8))
+    ref = model(prompt, use_cache=True)
+    hf.install(model)
+    streamed = hf.PackedDraftCache.empty(num_layers=2, residual=128)
+    out = model(prompt, past_key_values=streamed, use_cache=True)
+    assert torch.equal(out.logits, ref.logits)
+    after = hf.PackedDraftCache(ref.past_key_values, residual=128)
+    for i, layer in enumerate(ref.past_key_values.layers):
+        pk, pv = kvr.pack_kivi_kv(layer.keys, layer.values, k_bits=4, v_bits=4, group_size=32,
+                                  residual_length=128)
+        sk, sv = streamed.layers[i].packed.k, streamed.layers[i].packed.v
+        assert sk.prefix_length == pk.prefix_length == 640
+        assert torch.equal(sk.payload.reshape(-1), pk.payload.reshape(-1))
+        assert torch.equal(sk.scale.reshape(-1), pk.scale.reshape(-1))
+        assert torch.equal(sk.offset.reshape(-1), pk.offset.reshape(-1))
+        assert torch.equal(sk.residual, pk.residual)
+        assert torch.equal(sv.payload.reshape(-1), pv.payload.reshape(-1))
+        assert torch.equal(sv.scale.reshape(-1), pv.scale.reshape(-1))
+        assert torch.equal(sv.offset.reshape(-1), pv.offset.reshape(-1))
+    token = ref.logits[:, -1].argmax(-1, keepdim=True)
+    for _ in range(3):
+        a = model(token, past_key_values=streamed, use_cache=True).logits
+        b = model(token, past_key_values=after, use_cache=True).logits
+        assert torch.equal(a, b)
+        token = a[:, -1].argmax(-1, keepdim=True)
