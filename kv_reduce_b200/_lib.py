@@ -181,7 +181,13 @@ def call(fn: str, *args) -> None:
     check(fn, getattr(load(), fn)(*args))
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    """cudaStream_t of the current stream on `device` (as an int)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 

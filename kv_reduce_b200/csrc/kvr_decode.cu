@@ -927,6 +927,26 @@ static Plan make_plan(const kvr_decode_args* a, int tok_begin, int tok_end, int 
   return pl;
 }
 
+// make_plan memoised per host thread: a decode loop re-plans the same shape
+// every step (the cost model scans up to kMaxSplits candidates).
+static Plan cached_plan(const kvr_decode_args* a, int tb, int te, int occ) {
+  struct Entry {
+    int key[10];
+    Plan plan;
+  };
+  static thread_local Entry cache[8];
+  static thread_local int next = 0;
+  const int key[10] = {a->n_layers, a->batch, a->kv_heads, a->head_dim, tb, te, a->split_tokens,
+                       device_sms(a->num_sms), occ, 1};
+  for (auto& e : cache)
+    if (std::equal(key, key + 10, e.key)) return e.plan;
+  Entry& e = cache[next];
+  next = (next + 1) % 8;
+  std::copy(key, key + 10, e.key);
+  e.plan = make_plan(a, tb, te, occ);
+  return e.plan;
+}
+
 static int validate(const kvr_decode_args* a) {
   if (!a || !a->layers || a->n_layers < 1 || a->n_layers > KVR_MAX_LAYERS) return KVR_ERR_INVALID_ARGUMENT;
   if (a->batch < 1 || a->kv_heads < 1 || a->q_heads < 1 || a->q_heads % a->kv_heads) return KVR_ERR_INVALID_ARGUMENT;
@@ -1039,7 +1059,7 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
     // errors below still take precedence over the device error
     occ = std::max(1, std::min(C::MIN_CTAS, (228 * 1024) / (C::SMEM + 1024)));
   }
-  Plan pl = make_plan(a, tb, te, occ);
+  Plan pl = cached_plan(a, tb, te, occ);
   if (plan_only) { *plan_only = pl; return KVR_OK; }
   if (pl.num_splits > 1) {
     if (!a->workspace || a->workspace_bytes < pl.part_bytes || !a->counters) return KVR_ERR_WORKSPACE;

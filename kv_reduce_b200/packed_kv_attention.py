@@ -18,6 +18,7 @@ Differences from the reference, stated where a caller could notice them:
 from __future__ import annotations
 
 import ctypes
+import threading
 from dataclasses import dataclass
 from typing import Dict, List, Sequence, Tuple
 
@@ -146,6 +147,7 @@ def _layer_ptrs(query: torch.Tensor | None, out: torch.Tensor | None, k: PackedK
 # split-partial workspace is scratch that stream-ordered launches can share
 # the same way.  A launch object keeps references to the buffers it was
 # built with, so growing a cached buffer never frees memory still in use.
+_tls = threading.local()
 _COUNTERS: Dict[Tuple[int, int], torch.Tensor] = {}
 _WORKSPACE: Dict[Tuple[int, int], torch.Tensor] = {}
 _PLANS: Dict[tuple, Tuple[int, int, int]] = {}
@@ -266,9 +268,22 @@ def packed_kv_decode_attention(
     query = query.contiguous()
     geom = _geometry(query, packed_keys, packed_values)
     out_fp32 = out_dtype == torch.float32
-    out = torch.empty(query.shape, dtype=torch.float32 if out_fp32 else query.dtype, device=query.device)
-    launch = DecodeLaunch(geom, [_layer_ptrs(query, out, packed_keys, packed_values)], query.device,
-                          split_tokens=_effective_split(split_tokens, block_tokens), out_fp32=out_fp32)
+    out = torch.empty_like(query, dtype=torch.float32) if out_fp32 else torch.empty_like(query)
+    layer = _layer_ptrs(query, out, packed_keys, packed_values)
+    split = _effective_split(split_tokens, block_tokens)
+    stream = _lib.stream_ptr(query.device)
+    # one prepared launch per shape and stream, per host thread (the library
+    # call releases the GIL, so threads must not share an argument block)
+    cache = _tls.__dict__.setdefault("launches", {})
+    key = (geom, split, stream, out_fp32)
+    launch = cache.get(key)
+    if launch is None:
+        if len(cache) >= 64:
+            cache.clear()
+        launch = cache[key] = DecodeLaunch(geom, [layer], query.device, split_tokens=split, stream=stream,
+                                           out_fp32=out_fp32)
+    else:
+        launch.layers[0] = layer
     launch()
     return out
 
