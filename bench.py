@@ -52,6 +52,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--draft-loop", action="store_true",
+                   help="speculative draft loop on the streaming cache (use with --config 5)")
     p.add_argument("--split-sequence", action="store_true",
                    help="N>1: split ONE batch-1 sequence's tokens across the ranks (strong scaling, "
                         "partial decode + NCCL all-gather + LSE merge) instead of one sequence per rank")
@@ -522,6 +524,82 @@ def run_split_sequence(args, wl, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_draft_loop(args, wl, world, rank, local):
+    """Speculative draft loop on the streaming cache (default workload 5):
+    rounds of `draft_steps` steps, each step appending one token to every
+    layer and decoding over it.  Times the CUDA-graph replay of a round
+    (device-side lengths, one capture) against issuing the same launches
+    eagerly; each round is rolled back to the starting length so every round
+    sees the same cache.  Per rank: its own batch (weak scaling)."""
+    import torch.distributed as dist
+
+    import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import workloads
+    from kv_reduce_b200.draft import DraftLoop
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    steps = max(1, wl.draft_steps or 4)
+    cache = kvr.PackedKVCache(wl.layers, wl.batch, wl.kv_heads, wl.head_dim, k_bits=wl.k_bits, v_bits=wl.v_bits,
+                              group_size=wl.group_size, residual_length=wl.residual_length,
+                              capacity=wl.seq_len + 64, device=device)
+    seed_wl = wl.scaled(seed=wl.seed + 100 * rank)
+    for i, layer in enumerate(cache.layers):
+        k, v = workloads.make_layer_kv(seed_wl, i, device=device)
+        layer.prefill(k, v)
+        del k, v
+    loop = DraftLoop(cache, q_heads=wl.q_heads, steps=steps, split_tokens=args.split_tokens)
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    for t in (loop.q, loop.k, loop.v):
+        t.copy_(torch.randn(t.shape, generator=g, device=device).to(torch.bfloat16))
+    start = cache.get_seq_length()
+
+    def timed(fn):
+        ev = []
+        for i in range(max(args.warmup, 3) + args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            cache.crop(start)
+            if i >= max(args.warmup, 3):
+                ev.append((e0, e1))
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+        return max_over_ranks(ms, world, device)
+
+    graph_ms = timed(loop.replay)
+    eager_ms = timed(loop.run_eager)
+    errors = loop.errors()
+    # algorithmic bytes per draft step: the decode's bytes at the step's length
+    # plus the appended token (key row, value codes and metadata) per layer
+    step_bytes = sum(workloads.layer_bytes(wl, seq_len=start + t + 1)["total"] for t in range(steps)) / steps
+    step_bytes = step_bytes * wl.layers + wl.layers * wl.batch * wl.kv_heads * (
+        2 * wl.head_dim + wl.head_dim * wl.v_bits // 8 + 4)
+    us_step = graph_ms * 1e3 / steps
+    if rank == 0:
+        peak, peak_src = measured_peak()
+        line = {"metric": "draft loop: us per draft step (append + decode, all layers)", "value": us_step,
+                "unit": "us/step", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+                "dtype": "u4 codes; f16/bf16 mma, fp32 accumulate and softmax",
+                "data": "synthetic (seeded N(0,1) K/V/Q, outlier key channels)",
+                "config": {"workload": wl.name, "layers": wl.layers, "batch_per_gpu": wl.batch,
+                           "seq_len": start, "draft_steps": steps, "kv_bits": f"K{wl.k_bits}V{wl.v_bits}",
+                           "timing": "CUDA graph of one round (device-side lengths) vs the same launches "
+                                     "issued eagerly; CUDA events per round, rolled back between rounds"},
+                "graph_us_per_draft_step": us_step, "eager_us_per_draft_step": eager_ms * 1e3 / steps,
+                "achieved_gbs": step_bytes / (us_step * 1e-6) / 1e9 * world,
+                "frac_of_peak_per_gpu": step_bytes / (us_step * 1e-6) / 1e9 / peak, "peak_source": peak_src,
+                "append_errors": errors, "gpu_launches": args.steps * steps * wl.layers * 3}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     from kv_reduce_b200 import workloads
@@ -535,6 +613,9 @@ def main():
         return
     if args.split_sequence:
         run_split_sequence(args, wl, world, rank, local)
+        return
+    if args.draft_loop:
+        run_draft_loop(args, wl, world, rank, local)
         return
     run_ours(args, wl, world, rank, local)
 

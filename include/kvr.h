@@ -151,6 +151,19 @@ typedef struct {
 } kvr_flush_args;
 int kvr_flush_groups(const kvr_flush_args* a, kvr_stream_t stream);
 
+/* Lengths in device memory, for decode loops captured once in a CUDA graph
+ * and replayed at growing lengths (no reference counterpart: the reference
+ * passes lengths from the host on every call).  lengths is int[3]:
+ * [0] sequence length, [1] quantized prefix length, [2] error flag.
+ * kvr_append_lengths: kvr_append with seq_len / res_len read from lengths
+ *   at run time (a->seq_len, a->res_len ignored); an append past
+ *   a->seq_capacity or a->res_capacity writes nothing and sets lengths[2].
+ * kvr_advance_lengths: lengths[0] += n unless the error flag is set.
+ * kvr_set_lengths: lengths[0] = seq_len, lengths[1] = prefix_len.          */
+int kvr_append_lengths(const kvr_append_args* a, int* lengths, kvr_stream_t stream);
+int kvr_advance_lengths(int* lengths, int n, kvr_stream_t stream);
+int kvr_set_lengths(int* lengths, int seq_len, int prefix_len, kvr_stream_t stream);
+
 /* -------------------------------------------------------- decode attention
  * Replaces packed_kv_decode_attention (triton_packed_kv_attention.py:284-389)
  * and its three kernels (:27-131, :134-248, :251-281): one-token GQA decode
@@ -211,6 +224,17 @@ int kvr_decode_attention(const kvr_decode_args* a, kvr_stream_t stream);
  * shares the array and clears its counters; calls that overlap on the GPU
  * race.                                                                    */
 int kvr_decode_attention_noalloc(const kvr_decode_args* a, kvr_stream_t stream);
+
+/* kvr_decode_attention with the sequence and prefix lengths read from
+ * device memory at run time (lengths as for kvr_append_lengths).  a
+ * describes the capacity: a->seq_len = value rows the buffers hold (the
+ * split plan covers them; splits past the live length add nothing),
+ * a->prefix_len = key rows the payload/metadata buffers hold (a multiple
+ * of group_size), residual_capacity = rows of the BF16 key residual
+ * buffer.  The live lengths are clamped to those capacities.  No reference
+ * counterpart.                                                             */
+int kvr_decode_attention_lengths(const kvr_decode_args* a, const int* lengths, int residual_capacity,
+                                 kvr_stream_t stream);
 
 /* LSE merge of externally produced partials (the cross-GPU token split):
  * parts: n_parts blocks of [rows] (m, l) pairs and [rows, D] unnormalised

@@ -42,6 +42,10 @@ EXPORTED_SYMBOLS = (
     "kvr_lse_merge",
     "kvr_decode_partial",
     "kvr_decode_attention_noalloc",
+    "kvr_append_lengths",
+    "kvr_advance_lengths",
+    "kvr_set_lengths",
+    "kvr_decode_attention_lengths",
 )
 
 
@@ -161,6 +165,10 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_partial.argtypes = [POINTER(DecodeArgs), c_int, c_int, c_void_p, c_void_p, c_void_p]
     lib.kvr_lse_merge.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     lib.kvr_decode_attention_noalloc.argtypes = [POINTER(DecodeArgs), c_void_p]
+    lib.kvr_append_lengths.argtypes = [POINTER(AppendArgs), c_void_p, c_void_p]
+    lib.kvr_advance_lengths.argtypes = [c_void_p, c_int, c_void_p]
+    lib.kvr_set_lengths.argtypes = [c_void_p, c_int, c_int, c_void_p]
+    lib.kvr_decode_attention_lengths.argtypes = [POINTER(DecodeArgs), c_void_p, c_int, c_void_p]
     for name in EXPORTED_SYMBOLS:
         if name not in ("kvr_version", "kvr_status_string", "kvr_last_error"):
             getattr(lib, name).restype = c_int

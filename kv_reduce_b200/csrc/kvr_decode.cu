@@ -116,6 +116,8 @@ struct Params {
   int* cnt2;                     // [units]
   float* out_ml;                 // partial mode: (m, l) per (layer, b, hq)
   float* out_o;                  // partial mode: unnormalised o
+  const int* dev_len;            // non-null: sequence / prefix length read here at run time
+  int res_cap;                   // residual rows the key residual buffer holds
 };
 
 // ----------------------------------------------------------- register maps
@@ -327,8 +329,17 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
   const int dbase = t4 * (D / 4);
   const float NEG_INF = -__int_as_float(0x7f800000);
   const int NS = p.num_splits;
-  const int P = p.P, log2G = p.log2G;
-  const int t_end = p.tok_end;
+  const int log2G = p.log2G;
+  // Lengths: from the launch, or (graph-replayable loops) from device memory,
+  // clamped to the capacities the host validated: sequence <= tok_end,
+  // prefix <= P in whole groups, residual rows <= res_cap.
+  int P = p.P, t_end = p.tok_end;
+  if (p.dev_len) {
+    const int dl_s = *reinterpret_cast<const volatile int*>(p.dev_len);
+    const int dl_p = *reinterpret_cast<const volatile int*>(p.dev_len + 1);
+    P = min(max(dl_p, 0), p.P) >> log2G << log2G;
+    t_end = min(min(max(dl_s, P), p.tok_end), P + p.res_cap);
+  }
   uint8_t* ring = smem + warp * C::RING;
   const uint32_t ring_s = smem_u32(ring);
   uint4* qs = reinterpret_cast<uint4*>(smem + C::QS_OFF);
@@ -1020,6 +1031,8 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   p.cnt2 = a->counters ? a->counters + units * pl.groups1 : nullptr;
   p.out_ml = nullptr;
   p.out_o = nullptr;
+  p.dev_len = nullptr;
+  p.res_cap = a->seq_len - a->prefix_len;
 }
 
 // Per-device, per-instantiation set-up: dynamic shared memory limit and
@@ -1050,7 +1063,7 @@ static int prepare(int* ctas_per_sm) {
 
 template <int D, int KB, int VB>
 static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float* out_o, cudaStream_t s,
-                 Plan* plan_only) {
+                 Plan* plan_only, const int* dev_len, int res_cap) {
   using C = Cfg<D, KB, VB>;
   int occ = 3;
   const int dev_st = (a->n_layers == 1) ? prepare<D, KB, VB, 1>(&occ) : prepare<D, KB, VB, KVR_MAX_LAYERS>(&occ);
@@ -1070,24 +1083,26 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
     Params<1> p;
     fill_params(p, a, pl, tb, te);
     p.out_ml = out_ml; p.out_o = out_o;
+    if (dev_len) { p.dev_len = dev_len; p.res_cap = res_cap; }
     decode_kernel<D, KB, VB, 1><<<pl.grid, kWarps * 32, C::SMEM, s>>>(p);
   } else {
     Params<KVR_MAX_LAYERS> p;
     fill_params(p, a, pl, tb, te);
     p.out_ml = out_ml; p.out_o = out_o;
+    if (dev_len) { p.dev_len = dev_len; p.res_cap = res_cap; }
     decode_kernel<D, KB, VB, KVR_MAX_LAYERS><<<pl.grid, kWarps * 32, C::SMEM, s>>>(p);
   }
   return check_launch();
 }
 
 static int run(const kvr_decode_args* a, int tb, int te, float* out_ml, float* out_o, cudaStream_t s,
-               Plan* plan_only = nullptr) {
+               Plan* plan_only = nullptr, const int* dev_len = nullptr, int res_cap = 0) {
   int st = validate(a);
   if (st != KVR_OK) return st;
   if (tb < 0 || te > a->seq_len || tb >= te || tb % kChunk) return KVR_ERR_INVALID_ARGUMENT;
 #define KVR_CASE(D_, KB_, VB_)                                                              \
   if (a->head_dim == D_ && a->key_bits == KB_ && a->value_bits == VB_)                      \
-    return run_t<D_, KB_, VB_>(a, tb, te, out_ml, out_o, s, plan_only);
+    return run_t<D_, KB_, VB_>(a, tb, te, out_ml, out_o, s, plan_only, dev_len, res_cap);
   KVR_CASE(128, 4, 4) KVR_CASE(128, 8, 4) KVR_CASE(128, 4, 8) KVR_CASE(128, 8, 8)
   KVR_CASE(128, 2, 2) KVR_CASE(128, 2, 4) KVR_CASE(128, 4, 2) KVR_CASE(128, 8, 2) KVR_CASE(128, 2, 8)
   KVR_CASE(64, 4, 4) KVR_CASE(64, 8, 4) KVR_CASE(64, 4, 8) KVR_CASE(64, 8, 8) KVR_CASE(64, 2, 4)
@@ -1116,6 +1131,13 @@ extern "C" int kvr_decode_plan(const kvr_decode_args* a, int* num_splits, size_t
 extern "C" int kvr_decode_attention(const kvr_decode_args* a, kvr_stream_t stream) {
   if (!a) return KVR_ERR_INVALID_ARGUMENT;
   return dec::run(a, 0, a->seq_len, nullptr, nullptr, as_stream(stream));
+}
+
+extern "C" int kvr_decode_attention_lengths(const kvr_decode_args* a, const int* lengths, int residual_capacity,
+                                            kvr_stream_t stream) {
+  if (!a || !lengths || residual_capacity < 0) return KVR_ERR_INVALID_ARGUMENT;
+  if (a->seq_len - a->prefix_len > residual_capacity) return KVR_ERR_INVALID_ARGUMENT;
+  return dec::run(a, 0, a->seq_len, nullptr, nullptr, as_stream(stream), nullptr, lengths, residual_capacity);
 }
 
 extern "C" int kvr_decode_partial(const kvr_decode_args* a, int token_begin, int token_end, float* part_ml,

@@ -200,10 +200,22 @@ __global__ void dequant_kernel(kvr_dequant_args a, int flat_stream) {
 // ============================================================ streaming cache
 // Append: warp per (bh, new token).  Key row copied into the BF16 residual
 // window; value row quantized per token at row seq_len + i.
-__global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args a) {
+__global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args a, int* lengths) {
   __shared__ uint8_t codes_s[kTokWarps][kMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = a.head_dim, bits = a.value_bits;
+  if (lengths) {
+    // positions from device memory (graph-replayable loops); a step past
+    // either capacity sets the error flag lengths[2] and writes nothing
+    const int S = *reinterpret_cast<volatile int*>(lengths);
+    const int P = *reinterpret_cast<volatile int*>(lengths + 1);
+    if (P < 0 || P > S || S + a.n > a.seq_capacity || S - P + a.n > a.res_capacity) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(lengths + 2, 1);
+      return;
+    }
+    a.seq_len = S;
+    a.res_len = S - P;
+  }
   const int64_t row_bytes = (int64_t)D * bits / 8;
   const int64_t total = (int64_t)a.bh * a.n;
   for (int64_t item = (int64_t)blockIdx.x * kTokWarps + warp; item < total;
@@ -356,7 +368,43 @@ extern "C" int kvr_append(const kvr_append_args* a, kvr_stream_t stream) {
   if (!a->k || !a->v || !a->key_residual || !a->value_payload || !a->value_scale || !a->value_offset)
     return KVR_ERR_INVALID_ARGUMENT;
   const int64_t total = (int64_t)a->bh * a->n;
-  append_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, as_stream(stream)>>>(*a);
+  append_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, as_stream(stream)>>>(*a, nullptr);
+  return check_launch();
+}
+
+// ------------------------------------------------ lengths in device memory
+// lengths[0] = sequence length, lengths[1] = quantized prefix length,
+// lengths[2] = error flag (non-zero after an append past a capacity).
+__global__ void set_lengths_kernel(int* lengths, int seq_len, int prefix_len) {
+  lengths[0] = seq_len;
+  lengths[1] = prefix_len;
+}
+__global__ void advance_lengths_kernel(int* lengths, int n) {
+  if (lengths[2] == 0) lengths[0] += n;
+}
+
+extern "C" int kvr_append_lengths(const kvr_append_args* a, int* lengths, kvr_stream_t stream) {
+  if (!a || !lengths || a->head_dim <= 0 || a->head_dim > kMaxD || a->value_bits < 2 || a->value_bits > 8 ||
+      a->bh < 0 || a->n < 0 || a->res_capacity < 0 || a->seq_capacity < 0)
+    return KVR_ERR_INVALID_ARGUMENT;
+  if (((int64_t)a->head_dim * a->value_bits) % 8 != 0) return KVR_ERR_UNSUPPORTED;
+  if (a->bh == 0 || a->n == 0) return KVR_OK;
+  if (!a->k || !a->v || !a->key_residual || !a->value_payload || !a->value_scale || !a->value_offset)
+    return KVR_ERR_INVALID_ARGUMENT;
+  const int64_t total = (int64_t)a->bh * a->n;
+  append_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, as_stream(stream)>>>(*a, lengths);
+  return check_launch();
+}
+
+extern "C" int kvr_set_lengths(int* lengths, int seq_len, int prefix_len, kvr_stream_t stream) {
+  if (!lengths || seq_len < 0 || prefix_len < 0 || prefix_len > seq_len) return KVR_ERR_INVALID_ARGUMENT;
+  set_lengths_kernel<<<1, 1, 0, as_stream(stream)>>>(lengths, seq_len, prefix_len);
+  return check_launch();
+}
+
+extern "C" int kvr_advance_lengths(int* lengths, int n, kvr_stream_t stream) {
+  if (!lengths || n < 0) return KVR_ERR_INVALID_ARGUMENT;
+  advance_lengths_kernel<<<1, 1, 0, as_stream(stream)>>>(lengths, n);
   return check_launch();
 }
 

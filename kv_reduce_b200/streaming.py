@@ -53,6 +53,10 @@ class PackedKVCacheLayer:
         self.seq_len = 0
         self.prefix_len = 0
         self._cur = 0
+        # True: commit keeps the live residual in the same buffer (a captured
+        # CUDA graph holds its address); lengths mirrored on the device
+        self.pin_residual = False
+        self._dev_len: Optional[torch.Tensor] = None
         self._alloc(_round_up(max(int(capacity), 64), 64))
 
     # ------------------------------------------------------------ storage
@@ -137,6 +141,7 @@ class PackedKVCacheLayer:
             a.bh, a.rows, a.row0, a.head_dim, a.bits = bh, S, 0, D, self.v_bits
             _lib.call("kvr_quantize_per_token", a, self._stream())
         self.seq_len, self.prefix_len = S, P
+        self._sync_lengths()
 
     def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """Append n tokens: keys to the BF16 window, values quantized now."""
@@ -159,6 +164,7 @@ class PackedKVCacheLayer:
         a.head_dim, a.value_bits = self.head_dim, self.v_bits
         _lib.call("kvr_append", a, self._stream())
         self.seq_len += n
+        self._sync_lengths()
 
     def commit(self) -> int:
         """Promote full key groups out of the residual window; returns tokens promoted."""
@@ -178,8 +184,13 @@ class PackedKVCacheLayer:
         a.prefix_len, a.prefix_capacity = self.prefix_len, self.cap_prefix
         a.group_size, a.head_dim, a.key_bits = self.group_size, self.head_dim, self.k_bits
         _lib.call("kvr_flush_groups", a, self._stream())
-        self._cur = 1 - self._cur
         self.prefix_len += promoted
+        if self.pin_residual:
+            rest = res_len - promoted
+            src[:, :, :rest].copy_(dst[:, :, :rest])
+        else:
+            self._cur = 1 - self._cur
+        self._sync_lengths()
         return promoted
 
     def crop(self, length: int) -> None:
@@ -187,6 +198,21 @@ class PackedKVCacheLayer:
         if not (self.prefix_len <= length <= self.seq_len):
             raise ValueError(f"crop({length}) outside [{self.prefix_len}, {self.seq_len}].")
         self.seq_len = int(length)
+        self._sync_lengths()
+
+    # ------------------------------------------------- device-side lengths
+    def device_lengths(self) -> torch.Tensor:
+        """int32[3] on the device: (sequence length, prefix length, error
+        flag), kept equal to the host lengths by every host-side operation;
+        the graph-replayable append / advance / decode read and move it."""
+        if self._dev_len is None:
+            self._dev_len = torch.zeros(3, dtype=torch.int32, device=self.device)
+            self._sync_lengths()
+        return self._dev_len
+
+    def _sync_lengths(self) -> None:
+        if self._dev_len is not None:
+            _lib.call("kvr_set_lengths", self._dev_len.data_ptr(), self.seq_len, self.prefix_len, self._stream())
 
     def get_seq_length(self) -> int:
         return self.seq_len
