@@ -52,6 +52,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--nccl-exchange", action="store_true",
+                   help="--split-sequence: exchange partials with NCCL all-gather instead of the fused kernel")
     p.add_argument("--draft-loop", action="store_true",
                    help="speculative draft loop on the streaming cache (use with --config 5)")
     p.add_argument("--split-sequence", action="store_true",
@@ -479,11 +481,18 @@ def run_split_sequence(args, wl, world, rank, local):
     launch = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
                           split_tokens=args.split_tokens)
     out = torch.empty(rows, wl.head_dim, dtype=torch.bfloat16, device=device)
-    dec = kd.SequenceShardDecoder(rows, wl.head_dim, world, device, partial_fn=launch.partial,
-                                  merge_fn=lambda ml, o: kvr.lse_merge(ml, o, out=out))
+    p2p = world > 1 and not args.nccl_exchange
+    if p2p:
+        xchg = kd.PeerExchange(rows, wl.head_dim, device)
 
-    def step():
-        dec.step()
+        def step():
+            xchg.step(launch.partial)
+    else:
+        dec = kd.SequenceShardDecoder(rows, wl.head_dim, world, device, partial_fn=launch.partial,
+                                      merge_fn=lambda ml, o: kvr.lse_merge(ml, o, out=out))
+
+        def step():
+            dec.step()
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -514,11 +523,18 @@ def run_split_sequence(args, wl, world, rank, local):
                 "config": {"workload": wl.name, "layers": wl.layers, "global_batch": wl.batch,
                            "seq_len": wl.seq_len, "parallelism": f"token-split x{world}",
                            "shard_tokens": b - a, "num_splits": launch.num_splits,
-                           "timing": "eager: partial decode (all layers, one launch) + NCCL all-gather "
-                                     "+ LSE merge per step, CUDA events, max over ranks"},
+                           "exchange": ("one kernel: NVLink peer stores + signal + LSE merge" if p2p else
+                                        "NCCL all-gather + LSE merge launch" if world > 1 else "none"),
+                           "timing": "eager: partial decode (all layers, one launch) + exchange/merge "
+                                     "per step, CUDA events, max over ranks"},
                 "per_gpu_fraction_of_peak": value / world / peak, "peak_source": peak_src,
                 "gpu_launches": args.steps * 2}
         print(json.dumps(line), flush=True)
+    if p2p:
+        errors = xchg.errors()
+        xchg.close()
+        if errors:
+            raise SystemExit(f"rank {rank}: {errors} exchange wait(s) timed out")
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -251,6 +251,39 @@ int kvr_lse_merge(const float* part_ml, const float* part_o, int n_parts,
 int kvr_decode_partial(const kvr_decode_args* a, int token_begin, int token_end,
                        float* part_ml, float* part_o, kvr_stream_t stream);
 
+/* ----------------------------------------- cross-GPU exchange + merge
+ * Sequence-split decode across GPUs (no reference counterpart: the
+ * reference runs on one GPU): every rank holds partials (m, l, o) of its
+ * token shard from kvr_decode_partial; kvr_exchange_merge stores them into
+ * every peer's receive buffer over NVLink (CUDA IPC peer mappings), signals
+ * the peers, waits for theirs (bounded by timeout_ns; a time-out sets
+ * *error) and writes the LSE merge of all ranks as bf16 out[rows, D].
+ * Receive buffer of each rank: floats [2][world][rows*(2+D)] (halves
+ * alternate by step; per source: (m, l) [rows][2] then o [rows][D]) then
+ * int signal[world] at byte offset 8*world*rows*(2+D), 256 bytes reserved.
+ * epoch, counter and error start at zero; every rank makes the same calls
+ * in the same order.  The caller's partials for step n (n = 1, 2, ...) go
+ * into its own buffer's half n % 2, source slot rank.                      */
+typedef struct {
+  int world, rank, rows, head_dim;
+  float* const* recv;   /* device array [world]: each rank's receive buffer, as mapped here */
+  int* const* signal;   /* device array [world]: each rank's signal words, as mapped here */
+  int* epoch;           /* this rank, device: exchanges completed */
+  int* counter;         /* this rank, device: arrival counter */
+  int* error;           /* this rank, device: non-zero after a wait timed out */
+  uint16_t* out;        /* bf16 [rows, head_dim] */
+  long long timeout_ns;
+} kvr_exchange_args;
+int kvr_exchange_merge(const kvr_exchange_args* a, kvr_stream_t stream);
+
+/* Receive buffers shared between processes: device memory from cudaMalloc
+ * (zeroed) with a 64-byte CUDA IPC handle; a peer maps it with
+ * kvr_exchange_open and unmaps it with kvr_exchange_close.                 */
+int kvr_exchange_alloc(size_t bytes, void** ptr, unsigned char* handle);
+int kvr_exchange_open(const unsigned char* handle, void** ptr);
+int kvr_exchange_close(void* ptr);
+int kvr_exchange_free(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -46,6 +46,11 @@ EXPORTED_SYMBOLS = (
     "kvr_advance_lengths",
     "kvr_set_lengths",
     "kvr_decode_attention_lengths",
+    "kvr_exchange_merge",
+    "kvr_exchange_alloc",
+    "kvr_exchange_open",
+    "kvr_exchange_close",
+    "kvr_exchange_free",
 )
 
 
@@ -120,6 +125,14 @@ class LayerPtrs(Structure):
     ]
 
 
+class ExchangeArgs(Structure):
+    _fields_ = [
+        ("world", c_int), ("rank", c_int), ("rows", c_int), ("head_dim", c_int),
+        ("recv", c_void_p), ("signal", c_void_p), ("epoch", c_void_p), ("counter", c_void_p),
+        ("error", c_void_p), ("out", c_void_p), ("timeout_ns", ctypes.c_longlong),
+    ]
+
+
 class DecodeArgs(Structure):
     _fields_ = [
         ("layers", POINTER(LayerPtrs)), ("n_layers", c_int),
@@ -169,6 +182,11 @@ def load() -> ctypes.CDLL:
     lib.kvr_advance_lengths.argtypes = [c_void_p, c_int, c_void_p]
     lib.kvr_set_lengths.argtypes = [c_void_p, c_int, c_int, c_void_p]
     lib.kvr_decode_attention_lengths.argtypes = [POINTER(DecodeArgs), c_void_p, c_int, c_void_p]
+    lib.kvr_exchange_merge.argtypes = [POINTER(ExchangeArgs), c_void_p]
+    lib.kvr_exchange_alloc.argtypes = [c_size_t, POINTER(c_void_p), ctypes.c_char_p]
+    lib.kvr_exchange_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]
+    lib.kvr_exchange_close.argtypes = [c_void_p]
+    lib.kvr_exchange_free.argtypes = [c_void_p]
     for name in EXPORTED_SYMBOLS:
         if name not in ("kvr_version", "kvr_status_string", "kvr_last_error"):
             getattr(lib, name).restype = c_int

@@ -139,3 +139,104 @@ def empty_partial(ml: torch.Tensor, o: torch.Tensor) -> None:
     ml[:, 0].fill_(float("-inf"))
     ml[:, 1].zero_()
     o.zero_()
+
+
+class _DeviceMemory:
+    """A raw device range seen by torch.as_tensor (no copy, no ownership)."""
+
+    def __init__(self, ptr: int, shape: Tuple[int, ...], typestr: str) -> None:
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Fused cross-GPU exchange + LSE merge of sequence-split partials.
+
+    Every rank allocates a receive buffer, shares its CUDA IPC handle over the
+    process group and maps every peer's buffer.  A step writes this rank's
+    partials (partial_fn(ml [rows, 2], o [rows, D]), e.g. a DecodeLaunch's
+    ``partial``) into its own buffer, then ``kvr_exchange_merge`` pushes them
+    into every peer over NVLink, signals, waits for the peers (bounded by
+    ``timeout_s``) and merges all ranks into the bf16 output -- one kernel in
+    place of an all-gather collective and a merge launch.  All ranks make the
+    same calls in the same order; ``close()`` is collective too.
+    """
+
+    def __init__(self, rows: int, head_dim: int, device: torch.device, group=None,
+                 timeout_s: float = 2.0) -> None:
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.head_dim, self.device, self.group = int(rows), int(head_dim), device, group
+        slot = self.rows * (2 + self.head_dim)
+        data_bytes = 2 * self.world * slot * 4
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        _lib.call("kvr_exchange_alloc", data_bytes + 256, ctypes.byref(own), handle)
+        self._own = own.value
+        mine = torch.tensor(list(handle.raw), dtype=torch.uint8, device=device)
+        handles = torch.empty(self.world, 64, dtype=torch.uint8, device=device)
+        if dist.get_backend(group) == "nccl":
+            dist.all_gather_into_tensor(handles, mine, group=group)
+        else:
+            dist.all_gather(list(handles.unbind(0)), mine, group=group)
+        handles = handles.cpu()
+        self._peers: List[int] = []
+        for r in range(self.world):
+            if r == self.rank:
+                self._peers.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            _lib.call("kvr_exchange_open", bytes(handles[r].tolist()), ctypes.byref(p))
+            self._peers.append(p.value)
+        self.recv_ptrs = torch.tensor(self._peers, dtype=torch.int64, device=device)
+        self.signal_ptrs = self.recv_ptrs + data_bytes
+        self.state = torch.zeros(4, dtype=torch.int32, device=device)   # epoch, counter, error
+        self.out = torch.empty(self.rows, self.head_dim, dtype=torch.bfloat16, device=device)
+        self._views = []
+        for parity in (0, 1):
+            base = self._own + ((parity * self.world + self.rank) * slot) * 4
+            ml = torch.as_tensor(_DeviceMemory(base, (self.rows, 2), "<f4"), device=device)
+            o = torch.as_tensor(_DeviceMemory(base + 2 * self.rows * 4, (self.rows, self.head_dim), "<f4"),
+                                device=device)
+            self._views.append((ml, o))
+        st = self.state.data_ptr()
+        self._args = _lib.ExchangeArgs(self.world, self.rank, self.rows, self.head_dim, self.recv_ptrs.data_ptr(),
+                                       self.signal_ptrs.data_ptr(), st, st + 4, st + 8, self.out.data_ptr(),
+                                       int(timeout_s * 1e9))
+        self.steps = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+    def step(self, partial_fn: Callable[[torch.Tensor, torch.Tensor], None]) -> torch.Tensor:
+        from . import _lib
+
+        n = self.steps + 1
+        ml, o = self._views[n & 1]
+        partial_fn(ml, o)
+        _lib.call("kvr_exchange_merge", self._args, _lib.stream_ptr(self.device))
+        self.steps = n
+        return self.out
+
+    def errors(self) -> int:
+        """Non-zero if a wait for a peer timed out (synchronises)."""
+        return int(self.state[2].item())
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        from . import _lib
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for r, p in enumerate(self._peers):
+            if r != self.rank:
+                _lib.call("kvr_exchange_close", p)
+        dist.barrier(group=self.group)
+        _lib.call("kvr_exchange_free", self._own)
+        self._peers = []
