@@ -197,6 +197,299 @@ __global__ void dequant_kernel(kvr_dequant_args a, int flat_stream) {
   }
 }
 
+// ============================================== fast paths (2/4/8-bit codes)
+// Used when every packed row is whole bytes and the buffers are aligned for
+// vector accesses; the kernels above remain for everything else.  Same
+// arithmetic as the generic kernels, bit for bit.
+
+// Exact affine code with a reciprocal.  q = fl(x - mn) * fl(1/scale) is
+// within 1.5 * 2^-23 * q of the reference's quotient fl(fl(x - mn) / scale)
+// (< 5e-5 for codes up to 255), so both round to the same integer unless q
+// lies within that distance of n + 0.5; within 1e-3 of it the exact IEEE
+// division decides.
+__device__ __forceinline__ uint32_t affine_code_rcp(float x, float mn, float scale, float inv, int levels) {
+  const float diff = __fsub_rn(x, mn);
+  float q = __fmul_rn(diff, inv);
+  if (fabsf(q - floorf(q) - 0.5f) < 1e-3f) q = __fdiv_rn(diff, scale);
+  q = fminf(fmaxf(rintf(q), 0.f), (float)levels);
+  return (uint32_t)q;
+}
+
+// N bf16 values (N in {2, 4, 8}) as fp32, from one vector load.
+template <int N>
+__device__ __forceinline__ void load_bf16x(const uint16_t* p, float (&v)[N]) {
+  uint32_t w[N / 2];
+  if constexpr (N == 2) {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else if constexpr (N == 4) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    w[0] = x.x; w[1] = x.y;
+  } else {
+    const uint4 x = *reinterpret_cast<const uint4*>(p);
+    w[0] = x.x; w[1] = x.y; w[2] = x.z; w[3] = x.w;
+  }
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    v[2 * i] = bf16lo(w[i]);
+    v[2 * i + 1] = bf16hi(w[i]);
+  }
+}
+
+// Store the low NB bytes of `w` (NB in {1, 2, 4, 8}).
+template <int NB>
+__device__ __forceinline__ void store_bytes(uint8_t* p, uint64_t w) {
+  if constexpr (NB == 1) *p = (uint8_t)w;
+  else if constexpr (NB == 2) *reinterpret_cast<uint16_t*>(p) = (uint16_t)w;
+  else if constexpr (NB == 4) *reinterpret_cast<uint32_t*>(p) = (uint32_t)w;
+  else *reinterpret_cast<uint2*>(p) = make_uint2((uint32_t)w, (uint32_t)(w >> 32));
+}
+
+// Per-token values: a warp per row, lane l owns channels [l*K, l*K + K);
+// RPW rows per warp iteration keep several row loads in flight.
+template <int K, int BITS, int RPW>
+__global__ void __launch_bounds__(256) quant_token_fast(kvr_token_quant_args a) {
+  constexpr int LB = K * BITS / 8;   // packed bytes per lane
+  constexpr int levels = (1 << BITS) - 1;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t total = (int64_t)a.bh * a.rows;
+  for (int64_t base = warp0 * RPW; base < total; base += nwarps * RPW) {
+    float xv[RPW][K];
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+      const int64_t item = base + rr;
+      if (item < total) {
+        const int64_t bh = item / a.rows;
+        const int r = (int)(item - bh * a.rows);
+        load_bf16x<K>(a.x + bh * a.x_bh_stride + (int64_t)r * a.x_row_stride + lane * K, xv[rr]);
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+      const int64_t item = base + rr;
+      if (item >= total) break;   // warp-uniform
+      const int64_t bh = item / a.rows;
+      const int r = (int)(item - bh * a.rows);
+      float mn = xv[rr][0], mx = xv[rr][0];
+#pragma unroll
+      for (int k = 1; k < K; ++k) {
+        mn = fminf(mn, xv[rr][k]);
+        mx = fmaxf(mx, xv[rr][k]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      }
+      const float scale = affine_scale(mn, mx, BITS);
+      const float inv = __frcp_rn(scale);
+      uint64_t w = 0;
+#pragma unroll
+      for (int k = 0; k < K; ++k) w |= (uint64_t)affine_code_rcp(xv[rr][k], mn, scale, inv, levels) << (k * BITS);
+      store_bytes<LB>(a.payload + bh * a.payload_bh_stride + (int64_t)(a.row0 + r) * (32 * LB) + lane * LB, w);
+      if (lane == 0) {
+        const int64_t meta = bh * a.meta_bh_stride + a.row0 + r;
+        a.scale[meta] = f32_to_bf16_bits(scale);
+        a.offset[meta] = f32_to_bf16_bits(mn);
+      }
+    }
+  }
+}
+
+// Grouped keys (G <= 32): a thread per (b*h, group, channel quad); the
+// G x 4 bf16 values stay in registers, one 8-byte load per token row (a warp reads 32
+// consecutive quads of a row), one store of the packed quad per token.
+template <int G, int BITS>
+__global__ void __launch_bounds__(256) quant_group_fast(kvr_group_quant_args a) {
+  constexpr int QB = 4 * BITS / 8;   // packed bytes per quad
+  constexpr int levels = (1 << BITS) - 1;
+  const int D = a.head_dim, Q = D / 4;
+  const int64_t row_bytes = (int64_t)D * BITS / 8;
+  const int64_t total = (int64_t)a.bh * a.groups * Q;
+  for (int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tid < total;
+       tid += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t item = tid / Q;
+    const int j = (int)(tid - item * Q);
+    const int64_t bh = item / a.groups;
+    const int gi = (int)(item - bh * a.groups);
+    const int g = a.group0 + gi;
+    const uint16_t* x = a.x + bh * a.x_bh_stride + (int64_t)gi * G * a.x_row_stride + 4 * j;
+    uint2 raw[G];
+#pragma unroll
+    for (int t = 0; t < G; ++t) raw[t] = *reinterpret_cast<const uint2*>(x + (int64_t)t * a.x_row_stride);
+    float mn[4], mx[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t w0 = c < 2 ? raw[0].x : raw[0].y;
+      mn[c] = mx[c] = (c & 1) ? bf16hi(w0) : bf16lo(w0);
+    }
+#pragma unroll
+    for (int t = 1; t < G; ++t) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t w = c < 2 ? raw[t].x : raw[t].y;
+        const float v = (c & 1) ? bf16hi(w) : bf16lo(w);
+        mn[c] = fminf(mn[c], v);
+        mx[c] = fmaxf(mx[c], v);
+      }
+    }
+    float sc[4], inv[4];
+    uint32_t sbits[2] = {0u, 0u}, zbits[2] = {0u, 0u};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      sc[c] = affine_scale(mn[c], mx[c], BITS);
+      inv[c] = __frcp_rn(sc[c]);
+      sbits[c >> 1] |= (uint32_t)f32_to_bf16_bits(sc[c]) << (16 * (c & 1));
+      zbits[c >> 1] |= (uint32_t)f32_to_bf16_bits(mn[c]) << (16 * (c & 1));
+    }
+    const int64_t meta = bh * a.meta_bh_stride + (int64_t)g * D + 4 * j;
+    *reinterpret_cast<uint2*>(a.scale + meta) = make_uint2(sbits[0], sbits[1]);
+    *reinterpret_cast<uint2*>(a.offset + meta) = make_uint2(zbits[0], zbits[1]);
+    uint8_t* dst = a.payload + bh * a.payload_bh_stride + (int64_t)g * G * row_bytes + j * QB;
+#pragma unroll
+    for (int t = 0; t < G; ++t) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t wv = c < 2 ? raw[t].x : raw[t].y;
+        const float v = (c & 1) ? bf16hi(wv) : bf16lo(wv);
+        w |= affine_code_rcp(v, mn[c], sc[c], inv[c], levels) << (c * BITS);
+      }
+      store_bytes<QB>(dst + (int64_t)t * row_bytes, w);
+    }
+  }
+}
+
+// Dequantize: a thread per 8 consecutive outputs of a row (codes of the
+// 8 channels are BITS bytes; key metadata for them one 16-byte load each).
+template <int BITS, int OUT>
+__global__ void __launch_bounds__(256) dequant_fast(kvr_dequant_args a) {
+  const int D = a.head_dim, S = a.seq_len, C8 = D / 8;
+  const bool keys = a.group_size > 0;
+  const int P = keys ? a.prefix_len : S;
+  const int64_t row_bytes = (int64_t)D * BITS / 8;
+  const int64_t total = (int64_t)a.bh * S * C8;
+  for (int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tid < total;
+       tid += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = tid / C8;
+    const int c = (int)(tid - row * C8);
+    const int64_t bh = row / S;
+    const int t = (int)(row - bh * S);
+    float v[8];
+    if (t < P) {
+      const uint8_t* src = a.payload + bh * a.payload_bh_stride + (int64_t)t * row_bytes + (int64_t)c * BITS;
+      uint64_t w;
+      if constexpr (BITS == 2) w = *reinterpret_cast<const uint16_t*>(src);
+      else if constexpr (BITS == 4) w = *reinterpret_cast<const uint32_t*>(src);
+      else {
+        const uint2 x = *reinterpret_cast<const uint2*>(src);
+        w = (uint64_t)x.x | ((uint64_t)x.y << 32);
+      }
+      if (keys) {
+        const int64_t meta = bh * a.meta_bh_stride + (int64_t)(t / a.group_size) * D + 8 * c;
+        float s[8], z[8];
+        load_bf16x<8>(a.scale + meta, s);
+        load_bf16x<8>(a.offset + meta, z);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          v[i] = affine_dequant((uint32_t)(w >> (i * BITS)) & ((1u << BITS) - 1u), s[i], z[i]);
+      } else {
+        const int64_t meta = bh * a.meta_bh_stride + t;
+        const float s = bf16_bits_to_f32(a.scale[meta]), z = bf16_bits_to_f32(a.offset[meta]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = affine_dequant((uint32_t)(w >> (i * BITS)) & ((1u << BITS) - 1u), s, z);
+      }
+    } else {
+      load_bf16x<8>(a.residual + bh * a.residual_bh_stride + (int64_t)(t - P) * D + 8 * c, v);
+    }
+    const int64_t o = row * D + 8 * c;
+    if constexpr (OUT == 1) {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + o);
+      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      uint32_t h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (OUT == 2) {
+          const __half2 x = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+          h[i] = *reinterpret_cast<const uint32_t*>(&x);
+        } else {
+          h[i] = (uint32_t)f32_to_bf16_bits(v[2 * i]) | ((uint32_t)f32_to_bf16_bits(v[2 * i + 1]) << 16);
+        }
+      }
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + o) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+  }
+}
+
+// pack_unsigned / unpack_unsigned, 16 codes per thread; the last partial
+// group of 16 is handled byte by byte.
+template <int BITS>
+__global__ void pack_unsigned_fast(const uint8_t* __restrict__ codes, int64_t n, uint8_t* __restrict__ payload) {
+  constexpr uint32_t mask = (1u << BITS) - 1u;
+  const int64_t n16 = n / 16;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= n16; i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < n16) {
+      const uint4 c = reinterpret_cast<const uint4*>(codes)[i];
+      if constexpr (BITS == 8) {
+        reinterpret_cast<uint4*>(payload)[i] = c;   // 8-bit codes are their own stream
+      } else {
+        const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+        uint64_t w = 0;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) w |= (uint64_t)((cw[k >> 2] >> (8 * (k & 3))) & mask) << (k * BITS);
+        store_bytes<2 * BITS>(payload + i * (2 * BITS), w);
+      }
+    } else {
+      const int64_t b0 = n16 * 2 * BITS, nbytes = (n * BITS + 7) / 8;
+      for (int64_t b = b0; b < nbytes; ++b)
+        payload[b] = (uint8_t)stream_byte(b, BITS, n, [&](int64_t j) { return (uint32_t)codes[j]; });
+    }
+  }
+}
+
+template <int BITS>
+__global__ void unpack_unsigned_fast(const uint8_t* __restrict__ payload, int64_t n, uint8_t* __restrict__ codes) {
+  constexpr uint32_t mask = (1u << BITS) - 1u;
+  const int64_t n16 = n / 16;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= n16; i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < n16) {
+      const uint8_t* src = payload + i * (2 * BITS);
+      uint64_t w;
+      if constexpr (BITS == 2) w = *reinterpret_cast<const uint32_t*>(src);
+      else if constexpr (BITS == 4) {
+        const uint2 x = *reinterpret_cast<const uint2*>(src);
+        w = (uint64_t)x.x | ((uint64_t)x.y << 32);
+      } else {
+        w = 0;   // 8-bit codes are the payload itself
+      }
+      uint32_t out[4];
+      if constexpr (BITS == 8) {
+        const uint4 x = *reinterpret_cast<const uint4*>(src);
+        out[0] = x.x; out[1] = x.y; out[2] = x.z; out[3] = x.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t o = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) o |= (uint32_t)((w >> ((4 * q + k) * BITS)) & mask) << (8 * k);
+          out[q] = o;
+        }
+      }
+      reinterpret_cast<uint4*>(codes)[i] = make_uint4(out[0], out[1], out[2], out[3]);
+    } else {
+      for (int64_t j = n16 * 16; j < n; ++j) {
+        const int64_t bit = j * BITS;
+        codes[j] = (uint8_t)((payload[bit >> 3] >> (bit & 7)) & mask);
+      }
+    }
+  }
+}
+
+static inline bool al(const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
 // ============================================================ streaming cache
 // Append: warp per (bh, new token).  Key row copied into the BF16 residual
 // window; value row quantized per token at row seq_len + i.
@@ -285,6 +578,13 @@ extern "C" int kvr_pack_unsigned(const uint8_t* codes, int64_t n, int bits, uint
   if (n == 0) return KVR_OK;
   if (!codes || !payload) return KVR_ERR_INVALID_ARGUMENT;
   const int64_t nbytes = (n * bits + 7) / 8;
+  if ((bits == 2 || bits == 4 || bits == 8) && al(codes, 16) && al(payload, 16)) {
+    const int grid = grid_for(n / 16 + 1, 256);
+    if (bits == 2) pack_unsigned_fast<2><<<grid, 256, 0, as_stream(stream)>>>(codes, n, payload);
+    else if (bits == 4) pack_unsigned_fast<4><<<grid, 256, 0, as_stream(stream)>>>(codes, n, payload);
+    else pack_unsigned_fast<8><<<grid, 256, 0, as_stream(stream)>>>(codes, n, payload);
+    return check_launch();
+  }
   pack_unsigned_kernel<<<grid_for(nbytes, 256), 256, 0, as_stream(stream)>>>(codes, n, bits, payload, nbytes);
   return check_launch();
 }
@@ -295,6 +595,13 @@ extern "C" int kvr_unpack_unsigned(const uint8_t* payload, int64_t n, int bits, 
   if (n == 0) return KVR_OK;
   if (!codes || !payload) return KVR_ERR_INVALID_ARGUMENT;
   const int64_t nbytes = (n * bits + 7) / 8;
+  if ((bits == 2 || bits == 4 || bits == 8) && al(codes, 16) && al(payload, 16)) {
+    const int grid = grid_for(n / 16 + 1, 256);
+    if (bits == 2) unpack_unsigned_fast<2><<<grid, 256, 0, as_stream(stream)>>>(payload, n, codes);
+    else if (bits == 4) unpack_unsigned_fast<4><<<grid, 256, 0, as_stream(stream)>>>(payload, n, codes);
+    else unpack_unsigned_fast<8><<<grid, 256, 0, as_stream(stream)>>>(payload, n, codes);
+    return check_launch();
+  }
   unpack_unsigned_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(payload, nbytes, n, bits, codes);
   return check_launch();
 }
@@ -310,6 +617,21 @@ extern "C" int kvr_quantize_per_token(const kvr_token_quant_args* a, kvr_stream_
   // (payload_bh_stride is not used).
   if (generic && (!a->codes_scratch || a->row0 != 0)) return KVR_ERR_INVALID_ARGUMENT;
   const int64_t total = (int64_t)a->bh * a->rows;
+  {
+    const int D = a->head_dim, bits = a->bits, K = D / 32;
+    const bool fast = !generic && (bits == 2 || bits == 4 || bits == 8) && (D == 64 || D == 128 || D == 256) &&
+                      (K * bits) % 8 == 0 && al(a->x, 16) && a->x_bh_stride % K == 0 && a->x_row_stride % K == 0 &&
+                      al(a->payload, 16) && a->payload_bh_stride % 8 == 0;
+    if (fast) {
+      constexpr int RPW = 4;
+      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 8 * RPW - 1) / (8 * RPW), 148 * 64));
+#define KVR_TOK(K_, B_) \
+  if (K == K_ && bits == B_) quant_token_fast<K_, B_, RPW><<<grid, 256, 0, as_stream(stream)>>>(*a);
+      KVR_TOK(2, 4) KVR_TOK(2, 8) KVR_TOK(4, 2) KVR_TOK(4, 4) KVR_TOK(4, 8) KVR_TOK(8, 2) KVR_TOK(8, 4) KVR_TOK(8, 8)
+#undef KVR_TOK
+      return check_launch();
+    }
+  }
   quant_token_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, as_stream(stream)>>>(*a, generic);
   int st = check_launch();
   if (st != KVR_OK || !generic) return st;
@@ -332,6 +654,22 @@ extern "C" int kvr_quantize_grouped(const kvr_group_quant_args* a, kvr_stream_t 
     if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
   }
   const int64_t total = (int64_t)a->bh * a->groups;
+  {
+    const int D = a->head_dim, G = a->group_size, bits = a->bits;
+    const bool fast = !generic && (bits == 2 || bits == 4 || bits == 8) && D % 4 == 0 &&
+                      (G == 16 || G == 32) && al(a->x, 8) && a->x_bh_stride % 4 == 0 &&
+                      a->x_row_stride % 4 == 0 && al(a->payload, 4) && a->payload_bh_stride % 4 == 0 &&
+                      al(a->scale, 8) && al(a->offset, 8) && a->meta_bh_stride % 4 == 0;
+    if (fast) {
+      const int64_t threads_total = total * (D / 4);
+      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((threads_total + 255) / 256, 148 * 64));
+#define KVR_GRP(G_, B_) \
+  if (G == G_ && bits == B_) quant_group_fast<G_, B_><<<grid, 256, 0, as_stream(stream)>>>(*a);
+      KVR_GRP(16, 2) KVR_GRP(16, 4) KVR_GRP(16, 8) KVR_GRP(32, 2) KVR_GRP(32, 4) KVR_GRP(32, 8)
+#undef KVR_GRP
+      return check_launch();
+    }
+  }
   const int grid = (int)std::min<int64_t>(total, 148 * 16);
   quant_group_kernel<<<grid, threads, (size_t)smem, as_stream(stream)>>>(*a, generic);
   int st = check_launch();
@@ -354,6 +692,20 @@ extern "C" int kvr_dequantize(const kvr_dequant_args* a, kvr_stream_t stream) {
   if (keys && P < a->seq_len && !a->residual) return KVR_ERR_INVALID_ARGUMENT;
   const int flat = ((int64_t)a->head_dim * a->bits) % 8 != 0;
   const int64_t total = (int64_t)a->bh * a->seq_len * a->head_dim;
+  const int bits = a->bits, od = a->out_dtype;
+  const bool fast = !flat && (bits == 2 || bits == 4 || bits == 8) && a->head_dim % 8 == 0 && al(a->out, 16) &&
+                    (P == 0 || (al(a->payload, 8) && a->payload_bh_stride % 8 == 0)) &&
+                    (P == 0 || !keys || (al(a->scale, 16) && al(a->offset, 16) && a->meta_bh_stride % 8 == 0)) &&
+                    (P == a->seq_len || (al(a->residual, 16) && a->residual_bh_stride % 8 == 0));
+  if (fast) {
+    const int grid = grid_for(total / 8, 256);
+#define KVR_DQ(B_, O_) \
+  if (bits == B_ && od == O_) dequant_fast<B_, O_><<<grid, 256, 0, as_stream(stream)>>>(*a);
+    KVR_DQ(2, 0) KVR_DQ(2, 1) KVR_DQ(2, 2) KVR_DQ(4, 0) KVR_DQ(4, 1) KVR_DQ(4, 2) KVR_DQ(8, 0) KVR_DQ(8, 1)
+    KVR_DQ(8, 2)
+#undef KVR_DQ
+    return check_launch();
+  }
   dequant_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(*a, flat);
   return check_launch();
 }
