@@ -207,12 +207,15 @@ __global__ void dequant_kernel(kvr_dequant_args a, int flat_stream) {
 // (< 5e-5 for codes up to 255), so both round to the same integer unless q
 // lies within that distance of n + 0.5; within 1e-3 of it the exact IEEE
 // division decides.
+__device__ __noinline__ float exact_quotient(float diff, float scale) { return __fdiv_rn(diff, scale); }
+
 __device__ __forceinline__ uint32_t affine_code_rcp(float x, float mn, float scale, float inv, int levels) {
   const float diff = __fsub_rn(x, mn);
   float q = __fmul_rn(diff, inv);
-  if (fabsf(q - floorf(q) - 0.5f) < 1e-3f) q = __fdiv_rn(diff, scale);
-  q = fminf(fmaxf(rintf(q), 0.f), (float)levels);
-  return (uint32_t)q;
+  float r = rintf(q);
+  if (fabsf(q - r) > 0.5f - 1e-3f) r = rintf(exact_quotient(diff, scale));   // near n + 0.5: rare
+  r = fminf(fmaxf(r, 0.f), (float)levels);
+  return (uint32_t)r;
 }
 
 // N bf16 values (N in {2, 4, 8}) as fp32, from one vector load.
@@ -251,26 +254,24 @@ __global__ void __launch_bounds__(256) quant_token_fast(kvr_token_quant_args a) 
   constexpr int LB = K * BITS / 8;   // packed bytes per lane
   constexpr int levels = (1 << BITS) - 1;
   const int lane = threadIdx.x & 31;
-  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t total = (int64_t)a.bh * a.rows;
-  for (int64_t base = warp0 * RPW; base < total; base += nwarps * RPW) {
+  const int warp0 = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
+  const int bpb = (a.rows + RPW - 1) / RPW;   // row blocks per b*h slab
+  const int nblocks = a.bh * bpb;
+  for (int ib = warp0; ib < nblocks; ib += nwarps) {
+    const int bh = ib / bpb;
+    const int r0 = (ib - bh * bpb) * RPW;
+    const int nr = min(RPW, a.rows - r0);
+    const uint16_t* x = a.x + (int64_t)bh * a.x_bh_stride + (int64_t)r0 * a.x_row_stride + lane * K;
+    uint8_t* dst = a.payload + (int64_t)bh * a.payload_bh_stride + (int64_t)(a.row0 + r0) * (32 * LB) + lane * LB;
+    const int64_t meta0 = (int64_t)bh * a.meta_bh_stride + a.row0 + r0;
     float xv[RPW][K];
 #pragma unroll
-    for (int rr = 0; rr < RPW; ++rr) {
-      const int64_t item = base + rr;
-      if (item < total) {
-        const int64_t bh = item / a.rows;
-        const int r = (int)(item - bh * a.rows);
-        load_bf16x<K>(a.x + bh * a.x_bh_stride + (int64_t)r * a.x_row_stride + lane * K, xv[rr]);
-      }
-    }
+    for (int rr = 0; rr < RPW; ++rr)
+      if (rr < nr) load_bf16x<K>(x + (int64_t)rr * a.x_row_stride, xv[rr]);
 #pragma unroll
     for (int rr = 0; rr < RPW; ++rr) {
-      const int64_t item = base + rr;
-      if (item >= total) break;   // warp-uniform
-      const int64_t bh = item / a.rows;
-      const int r = (int)(item - bh * a.rows);
+      if (rr >= nr) break;   // warp-uniform
       float mn = xv[rr][0], mx = xv[rr][0];
 #pragma unroll
       for (int k = 1; k < K; ++k) {
@@ -287,51 +288,47 @@ __global__ void __launch_bounds__(256) quant_token_fast(kvr_token_quant_args a) 
       uint64_t w = 0;
 #pragma unroll
       for (int k = 0; k < K; ++k) w |= (uint64_t)affine_code_rcp(xv[rr][k], mn, scale, inv, levels) << (k * BITS);
-      store_bytes<LB>(a.payload + bh * a.payload_bh_stride + (int64_t)(a.row0 + r) * (32 * LB) + lane * LB, w);
+      store_bytes<LB>(dst + (int64_t)rr * (32 * LB), w);
       if (lane == 0) {
-        const int64_t meta = bh * a.meta_bh_stride + a.row0 + r;
-        a.scale[meta] = f32_to_bf16_bits(scale);
-        a.offset[meta] = f32_to_bf16_bits(mn);
+        a.scale[meta0 + rr] = f32_to_bf16_bits(scale);
+        a.offset[meta0 + rr] = f32_to_bf16_bits(mn);
       }
     }
   }
 }
 
-// Grouped keys (G <= 32): a thread per (b*h, group, channel quad); the
-// G x 4 bf16 values stay in registers, one 8-byte load per token row (a warp reads 32
-// consecutive quads of a row), one store of the packed quad per token.
+// Grouped keys (G <= 32): a thread per (b*h, group, channel quad); a first
+// pass over the group's G rows takes the per-channel min/max (one 8-byte
+// load per row; a warp reads 32 consecutive quads of a row), the second
+// re-reads them (L1) to emit the codes, one store of the packed quad per row.
 template <int G, int BITS>
 __global__ void __launch_bounds__(256) quant_group_fast(kvr_group_quant_args a) {
   constexpr int QB = 4 * BITS / 8;   // packed bytes per quad
   constexpr int levels = (1 << BITS) - 1;
   const int D = a.head_dim, Q = D / 4;
-  const int64_t row_bytes = (int64_t)D * BITS / 8;
-  const int64_t total = (int64_t)a.bh * a.groups * Q;
-  for (int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tid < total;
-       tid += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t item = tid / Q;
-    const int j = (int)(tid - item * Q);
-    const int64_t bh = item / a.groups;
-    const int gi = (int)(item - bh * a.groups);
+  const int row_bytes = D * BITS / 8;
+  const int total = a.bh * a.groups * Q;
+  for (int tid = blockIdx.x * blockDim.x + threadIdx.x; tid < total; tid += gridDim.x * blockDim.x) {
+    const int item = tid / Q;
+    const int j = tid - item * Q;
+    const int bh = item / a.groups;
+    const int gi = item - bh * a.groups;
     const int g = a.group0 + gi;
-    const uint16_t* x = a.x + bh * a.x_bh_stride + (int64_t)gi * G * a.x_row_stride + 4 * j;
-    uint2 raw[G];
-#pragma unroll
-    for (int t = 0; t < G; ++t) raw[t] = *reinterpret_cast<const uint2*>(x + (int64_t)t * a.x_row_stride);
+    const uint16_t* x = a.x + (int64_t)bh * a.x_bh_stride + (int64_t)gi * G * a.x_row_stride + 4 * j;
     float mn[4], mx[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t w0 = c < 2 ? raw[0].x : raw[0].y;
-      mn[c] = mx[c] = (c & 1) ? bf16hi(w0) : bf16lo(w0);
+    {
+      const uint2 w = __ldg(reinterpret_cast<const uint2*>(x));
+      mn[0] = mx[0] = bf16lo(w.x); mn[1] = mx[1] = bf16hi(w.x);
+      mn[2] = mx[2] = bf16lo(w.y); mn[3] = mx[3] = bf16hi(w.y);
     }
-#pragma unroll
+#pragma unroll 8
     for (int t = 1; t < G; ++t) {
+      const uint2 w = __ldg(reinterpret_cast<const uint2*>(x + (int64_t)t * a.x_row_stride));
+      const float v[4] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y)};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const uint32_t w = c < 2 ? raw[t].x : raw[t].y;
-        const float v = (c & 1) ? bf16hi(w) : bf16lo(w);
-        mn[c] = fminf(mn[c], v);
-        mx[c] = fmaxf(mx[c], v);
+        mn[c] = fminf(mn[c], v[c]);
+        mx[c] = fmaxf(mx[c], v[c]);
       }
     }
     float sc[4], inv[4];
@@ -343,20 +340,18 @@ __global__ void __launch_bounds__(256) quant_group_fast(kvr_group_quant_args a) 
       sbits[c >> 1] |= (uint32_t)f32_to_bf16_bits(sc[c]) << (16 * (c & 1));
       zbits[c >> 1] |= (uint32_t)f32_to_bf16_bits(mn[c]) << (16 * (c & 1));
     }
-    const int64_t meta = bh * a.meta_bh_stride + (int64_t)g * D + 4 * j;
+    const int64_t meta = (int64_t)bh * a.meta_bh_stride + (int64_t)g * D + 4 * j;
     *reinterpret_cast<uint2*>(a.scale + meta) = make_uint2(sbits[0], sbits[1]);
     *reinterpret_cast<uint2*>(a.offset + meta) = make_uint2(zbits[0], zbits[1]);
-    uint8_t* dst = a.payload + bh * a.payload_bh_stride + (int64_t)g * G * row_bytes + j * QB;
-#pragma unroll
+    uint8_t* dst = a.payload + (int64_t)bh * a.payload_bh_stride + (int64_t)g * G * row_bytes + j * QB;
+#pragma unroll 8
     for (int t = 0; t < G; ++t) {
-      uint32_t w = 0;
+      const uint2 w = __ldg(reinterpret_cast<const uint2*>(x + (int64_t)t * a.x_row_stride));
+      const float v[4] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y)};
+      uint32_t word = 0;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint32_t wv = c < 2 ? raw[t].x : raw[t].y;
-        const float v = (c & 1) ? bf16hi(wv) : bf16lo(wv);
-        w |= affine_code_rcp(v, mn[c], sc[c], inv[c], levels) << (c * BITS);
-      }
-      store_bytes<QB>(dst + (int64_t)t * row_bytes, w);
+      for (int c = 0; c < 4; ++c) word |= affine_code_rcp(v[c], mn[c], sc[c], inv[c], levels) << (c * BITS);
+      store_bytes<QB>(dst + (int64_t)t * row_bytes, word);
     }
   }
 }
@@ -369,16 +364,15 @@ __global__ void __launch_bounds__(256) dequant_fast(kvr_dequant_args a) {
   const bool keys = a.group_size > 0;
   const int P = keys ? a.prefix_len : S;
   const int64_t row_bytes = (int64_t)D * BITS / 8;
-  const int64_t total = (int64_t)a.bh * S * C8;
-  for (int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tid < total;
-       tid += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = tid / C8;
-    const int c = (int)(tid - row * C8);
-    const int64_t bh = row / S;
-    const int t = (int)(row - bh * S);
+  const int total = a.bh * S * C8;   // < 2^31 (checked by the launcher)
+  for (int tid = blockIdx.x * blockDim.x + threadIdx.x; tid < total; tid += gridDim.x * blockDim.x) {
+    const int row = tid / C8;
+    const int c = tid - row * C8;
+    const int bh = row / S;
+    const int t = row - bh * S;
     float v[8];
     if (t < P) {
-      const uint8_t* src = a.payload + bh * a.payload_bh_stride + (int64_t)t * row_bytes + (int64_t)c * BITS;
+      const uint8_t* src = a.payload + (int64_t)bh * a.payload_bh_stride + (int64_t)t * row_bytes + (int64_t)c * BITS;
       uint64_t w;
       if constexpr (BITS == 2) w = *reinterpret_cast<const uint16_t*>(src);
       else if constexpr (BITS == 4) w = *reinterpret_cast<const uint32_t*>(src);
@@ -387,7 +381,7 @@ __global__ void __launch_bounds__(256) dequant_fast(kvr_dequant_args a) {
         w = (uint64_t)x.x | ((uint64_t)x.y << 32);
       }
       if (keys) {
-        const int64_t meta = bh * a.meta_bh_stride + (int64_t)(t / a.group_size) * D + 8 * c;
+        const int64_t meta = (int64_t)bh * a.meta_bh_stride + (int64_t)(t / a.group_size) * D + 8 * c;
         float s[8], z[8];
         load_bf16x<8>(a.scale + meta, s);
         load_bf16x<8>(a.offset + meta, z);
@@ -395,15 +389,15 @@ __global__ void __launch_bounds__(256) dequant_fast(kvr_dequant_args a) {
         for (int i = 0; i < 8; ++i)
           v[i] = affine_dequant((uint32_t)(w >> (i * BITS)) & ((1u << BITS) - 1u), s[i], z[i]);
       } else {
-        const int64_t meta = bh * a.meta_bh_stride + t;
+        const int64_t meta = (int64_t)bh * a.meta_bh_stride + t;
         const float s = bf16_bits_to_f32(a.scale[meta]), z = bf16_bits_to_f32(a.offset[meta]);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = affine_dequant((uint32_t)(w >> (i * BITS)) & ((1u << BITS) - 1u), s, z);
       }
     } else {
-      load_bf16x<8>(a.residual + bh * a.residual_bh_stride + (int64_t)(t - P) * D + 8 * c, v);
+      load_bf16x<8>(a.residual + (int64_t)bh * a.residual_bh_stride + (int64_t)(t - P) * D + 8 * c, v);
     }
-    const int64_t o = row * D + 8 * c;
+    const int64_t o = (int64_t)row * D + 8 * c;
     if constexpr (OUT == 1) {
       float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + o);
       dst[0] = make_float4(v[0], v[1], v[2], v[3]);
@@ -619,7 +613,8 @@ extern "C" int kvr_quantize_per_token(const kvr_token_quant_args* a, kvr_stream_
   const int64_t total = (int64_t)a->bh * a->rows;
   {
     const int D = a->head_dim, bits = a->bits, K = D / 32;
-    const bool fast = !generic && (bits == 2 || bits == 4 || bits == 8) && (D == 64 || D == 128 || D == 256) &&
+    const bool fast = !generic && total < (1ll << 30) && (bits == 2 || bits == 4 || bits == 8) &&
+                      (D == 64 || D == 128 || D == 256) &&
                       (K * bits) % 8 == 0 && al(a->x, 16) && a->x_bh_stride % K == 0 && a->x_row_stride % K == 0 &&
                       al(a->payload, 16) && a->payload_bh_stride % 8 == 0;
     if (fast) {
@@ -656,7 +651,8 @@ extern "C" int kvr_quantize_grouped(const kvr_group_quant_args* a, kvr_stream_t 
   const int64_t total = (int64_t)a->bh * a->groups;
   {
     const int D = a->head_dim, G = a->group_size, bits = a->bits;
-    const bool fast = !generic && (bits == 2 || bits == 4 || bits == 8) && D % 4 == 0 &&
+    const bool fast = !generic && total * (D / 4) < (1ll << 30) && (bits == 2 || bits == 4 || bits == 8) &&
+                      D % 4 == 0 &&
                       (G == 16 || G == 32) && al(a->x, 8) && a->x_bh_stride % 4 == 0 &&
                       a->x_row_stride % 4 == 0 && al(a->payload, 4) && a->payload_bh_stride % 4 == 0 &&
                       al(a->scale, 8) && al(a->offset, 8) && a->meta_bh_stride % 4 == 0;
@@ -693,7 +689,8 @@ extern "C" int kvr_dequantize(const kvr_dequant_args* a, kvr_stream_t stream) {
   const int flat = ((int64_t)a->head_dim * a->bits) % 8 != 0;
   const int64_t total = (int64_t)a->bh * a->seq_len * a->head_dim;
   const int bits = a->bits, od = a->out_dtype;
-  const bool fast = !flat && (bits == 2 || bits == 4 || bits == 8) && a->head_dim % 8 == 0 && al(a->out, 16) &&
+  const bool fast = !flat && total / 8 < (1ll << 30) && (bits == 2 || bits == 4 || bits == 8) &&
+                    a->head_dim % 8 == 0 && al(a->out, 16) &&
                     (P == 0 || (al(a->payload, 8) && a->payload_bh_stride % 8 == 0)) &&
                     (P == 0 || !keys || (al(a->scale, 16) && al(a->offset, 16) && a->meta_bh_stride % 8 == 0)) &&
                     (P == a->seq_len || (al(a->residual, 16) && a->residual_bh_stride % 8 == 0));
