@@ -494,18 +494,35 @@ def run_split_sequence(args, wl, world, rank, local):
         def step():
             dec.step()
 
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(2 * ((max(args.warmup, 3) + 1) // 2)):   # an even number: the graph pairs steps
         step()
     torch.cuda.synchronize()
+    graph = None
+    if p2p:
+        # both steps of a pair (one per receive half) in one CUDA graph, the
+        # partial launch bound to the capture stream
+        side = torch.cuda.Stream(device)
+        launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
+                                split_tokens=args.split_tokens, stream=side.cuda_stream)
+        graph = xchg.capture_pair(launch_g.partial, side)
+        for _ in range(2):
+            xchg.replay_pair(graph)
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    pairs = max(1, args.steps // 2)
+    n_steps = 2 * pairs if graph is not None else args.steps
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s0.record()
-    for _ in range(args.steps):
-        step()
+    if graph is not None:
+        for _ in range(pairs):
+            xchg.replay_pair(graph)
+    else:
+        for _ in range(args.steps):
+            step()
     s1.record()
     torch.cuda.synchronize()
-    ms = s0.elapsed_time(s1) / args.steps
+    ms = s0.elapsed_time(s1) / n_steps
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -515,7 +532,7 @@ def run_split_sequence(args, wl, world, rank, local):
     if rank == 0:
         peak, peak_src = measured_peak()
         value = step_bytes / (ms * 1e-3) / 1e9
-        line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": n_steps,
                 "warmup": args.warmup, "ms_per_step": ms, "us_per_step": ms * 1e3,
                 "tokens_per_s": wl.batch / (ms * 1e-3), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "u4 codes; f16/bf16 mma, fp32 accumulate and softmax",
@@ -525,13 +542,16 @@ def run_split_sequence(args, wl, world, rank, local):
                            "shard_tokens": b - a, "num_splits": launch.num_splits,
                            "exchange": ("one kernel: NVLink peer stores + signal + LSE merge" if p2p else
                                         "NCCL all-gather + LSE merge launch" if world > 1 else "none"),
-                           "timing": "eager: partial decode (all layers, one launch) + exchange/merge "
-                                     "per step, CUDA events, max over ranks"},
+                           "timing": ("CUDA graph of two steps (partial decode of all layers + fused exchange)"
+                                      if graph is not None else
+                                      "eager: partial decode (all layers, one launch) + exchange/merge per step")
+                                     + ", CUDA events, max over ranks"},
                 "per_gpu_fraction_of_peak": value / world / peak, "peak_source": peak_src,
                 "gpu_launches": args.steps * 2}
         print(json.dumps(line), flush=True)
     if p2p:
         errors = xchg.errors()
+        del graph
         xchg.close()
         if errors:
             raise SystemExit(f"rank {rank}: {errors} exchange wait(s) timed out")

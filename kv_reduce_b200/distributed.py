@@ -223,6 +223,28 @@ class PeerExchange:
         self.steps = n
         return self.out
 
+    def capture_pair(self, partial_fn: Callable[[torch.Tensor, torch.Tensor], None],
+                     stream: torch.cuda.Stream) -> torch.cuda.CUDAGraph:
+        """Record two consecutive steps -- one per receive half -- into a CUDA
+        graph on `stream` (partial_fn must launch on the current stream).  The
+        exchange kernel reads its epoch from device memory, so the graph can
+        be replayed any number of times with ``replay_pair``; every rank
+        records and replays its pair in step with the others."""
+        if self.steps % 2:
+            raise ValueError("capture after an even number of steps")
+        g = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.graph(g, stream=stream):
+            self.step(partial_fn)
+            self.step(partial_fn)
+        self.steps -= 2   # they run when the graph is replayed
+        return g
+
+    def replay_pair(self, graph: torch.cuda.CUDAGraph) -> torch.Tensor:
+        graph.replay()
+        self.steps += 2
+        return self.out
+
     def errors(self) -> int:
         """Non-zero if a wait for a peer timed out (synchronises)."""
         return int(self.state[2].item())
