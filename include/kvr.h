@@ -153,14 +153,16 @@ int kvr_flush_groups(const kvr_flush_args* a, kvr_stream_t stream);
 
 /* Lengths in device memory, for decode loops captured once in a CUDA graph
  * and replayed at growing lengths (no reference counterpart: the reference
- * passes lengths from the host on every call).  lengths is int[3]:
- * [0] sequence length, [1] quantized prefix length, [2] error flag.
+ * passes lengths from the host on every call).  lengths is int[4]:
+ * [0] sequence length, [1] quantized prefix length, [2] error flag,
+ * [3] zero (scratch of the append's arrival count).
  * kvr_append_lengths: kvr_append with seq_len / res_len read from lengths
  *   at run time (a->seq_len, a->res_len ignored); an append past
- *   a->seq_capacity or a->res_capacity writes nothing and sets lengths[2].
+ *   a->seq_capacity or a->res_capacity writes nothing and sets lengths[2];
+ *   advance != 0: lengths[0] += a->n once the append is complete.
  * kvr_advance_lengths: lengths[0] += n unless the error flag is set.
  * kvr_set_lengths: lengths[0] = seq_len, lengths[1] = prefix_len.          */
-int kvr_append_lengths(const kvr_append_args* a, int* lengths, kvr_stream_t stream);
+int kvr_append_lengths(const kvr_append_args* a, int* lengths, int advance, kvr_stream_t stream);
 int kvr_advance_lengths(int* lengths, int n, kvr_stream_t stream);
 int kvr_set_lengths(int* lengths, int seq_len, int prefix_len, kvr_stream_t stream);
 

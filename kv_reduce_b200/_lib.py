@@ -178,7 +178,7 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_partial.argtypes = [POINTER(DecodeArgs), c_int, c_int, c_void_p, c_void_p, c_void_p]
     lib.kvr_lse_merge.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     lib.kvr_decode_attention_noalloc.argtypes = [POINTER(DecodeArgs), c_void_p]
-    lib.kvr_append_lengths.argtypes = [POINTER(AppendArgs), c_void_p, c_void_p]
+    lib.kvr_append_lengths.argtypes = [POINTER(AppendArgs), c_void_p, c_int, c_void_p]
     lib.kvr_advance_lengths.argtypes = [c_void_p, c_int, c_void_p]
     lib.kvr_set_lengths.argtypes = [c_void_p, c_int, c_int, c_void_p]
     lib.kvr_decode_attention_lengths.argtypes = [POINTER(DecodeArgs), c_void_p, c_int, c_void_p]

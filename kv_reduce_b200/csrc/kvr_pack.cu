@@ -487,7 +487,20 @@ static inline bool al(const void* p, int n) { return (reinterpret_cast<uintptr_t
 // ============================================================ streaming cache
 // Append: warp per (bh, new token).  Key row copied into the BF16 residual
 // window; value row quantized per token at row seq_len + i.
-__global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args a, int* lengths) {
+// After an append from device-side lengths: the last block to finish moves
+// the sequence length on by n (lengths[3] counts finished blocks, left zero).
+__device__ __forceinline__ void advance_after_append(int* lengths, int n) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(lengths + 3, 1) == (int)gridDim.x - 1) {
+      lengths[3] = 0;
+      lengths[0] += n;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args a, int* lengths, int advance) {
   __shared__ uint8_t codes_s[kTokWarps][kMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = a.head_dim, bits = a.value_bits;
@@ -547,6 +560,66 @@ __global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args 
       dst[b] = (uint8_t)stream_byte(b, bits, D, [&](int64_t j) { return (uint32_t)codes_s[warp][j]; });
     __syncwarp();
   }
+  if (lengths && advance) advance_after_append(lengths, a.n);
+}
+
+// Append, vectorised (D in {64,128,256}, 2/4/8-bit values): a warp per new
+// token row; lane l copies key channels [l*K, l*K+K) and quantizes the same
+// value channels in registers (as quant_token_fast).
+template <int K, int BITS>
+__global__ void __launch_bounds__(256) append_fast(kvr_append_args a, int* lengths, int advance) {
+  constexpr int LB = K * BITS / 8;
+  constexpr int levels = (1 << BITS) - 1;
+  const int lane = threadIdx.x & 31;
+  if (lengths) {
+    const int S = *reinterpret_cast<volatile int*>(lengths);
+    const int P = *reinterpret_cast<volatile int*>(lengths + 1);
+    if (P < 0 || P > S || S + a.n > a.seq_capacity || S - P + a.n > a.res_capacity) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(lengths + 2, 1);
+      return;
+    }
+    a.seq_len = S;
+    a.res_len = S - P;
+  }
+  const int total = a.bh * a.n;
+  const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
+  for (int item = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); item < total; item += nwarps) {
+    const int bh = item / a.n;
+    const int i = item - bh * a.n;
+    const int64_t src = (int64_t)item * (32 * K) + lane * K;
+    // key row -> BF16 residual window (K bf16 per lane)
+    uint16_t* kr = a.key_residual + (int64_t)bh * a.key_residual_bh_stride + (int64_t)(a.res_len + i) * (32 * K) +
+                   lane * K;
+    if constexpr (K == 2) *reinterpret_cast<uint32_t*>(kr) = *reinterpret_cast<const uint32_t*>(a.k + src);
+    else if constexpr (K == 4) *reinterpret_cast<uint2*>(kr) = *reinterpret_cast<const uint2*>(a.k + src);
+    else *reinterpret_cast<uint4*>(kr) = *reinterpret_cast<const uint4*>(a.k + src);
+    float xv[K];
+    load_bf16x<K>(a.v + src, xv);
+    float mn = xv[0], mx = xv[0];
+#pragma unroll
+    for (int k = 1; k < K; ++k) {
+      mn = fminf(mn, xv[k]);
+      mx = fmaxf(mx, xv[k]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const float scale = affine_scale(mn, mx, BITS);
+    const float inv = __frcp_rn(scale);
+    uint64_t w = 0;
+#pragma unroll
+    for (int k = 0; k < K; ++k) w |= (uint64_t)affine_code_rcp(xv[k], mn, scale, inv, levels) << (k * BITS);
+    store_bytes<LB>(a.value_payload + (int64_t)bh * a.value_payload_bh_stride + (int64_t)(a.seq_len + i) * (32 * LB) +
+                        lane * LB, w);
+    if (lane == 0) {
+      const int64_t meta = (int64_t)bh * a.value_meta_bh_stride + a.seq_len + i;
+      a.value_scale[meta] = f32_to_bf16_bits(scale);
+      a.value_offset[meta] = f32_to_bf16_bits(mn);
+    }
+  }
+  if (lengths && advance) advance_after_append(lengths, a.n);
 }
 
 // Residual window shift after a flush: rows [shift, res_len) -> [0, ..).
@@ -559,6 +632,26 @@ __global__ void residual_move_kernel(const uint16_t* __restrict__ src, uint16_t*
     const int64_t b = i / per, r = i % per;
     dst[b * bh_stride + r] = src[b * bh_stride + (int64_t)shift * D + r];
   }
+}
+
+// Append launcher: the vectorised kernel where the layout allows it.
+static int launch_append(const kvr_append_args* a, int* lengths, int advance, cudaStream_t s) {
+  const int64_t total = (int64_t)a->bh * a->n;
+  const int D = a->head_dim, bits = a->value_bits, K = D / 32;
+  const bool fast = total < (1ll << 30) && (D == 64 || D == 128 || D == 256) && (bits == 2 || bits == 4 || bits == 8) &&
+                    (K * bits) % 8 == 0 && al(a->k, 16) && al(a->v, 16) && al(a->key_residual, 16) &&
+                    a->key_residual_bh_stride % 8 == 0 && al(a->value_payload, 16) &&
+                    a->value_payload_bh_stride % 8 == 0;
+  if (fast) {
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 7) / 8, 148 * 64));
+#define KVR_APP(K_, B_) \
+  if (K == K_ && bits == B_) append_fast<K_, B_><<<grid, 256, 0, s>>>(*a, lengths, advance);
+    KVR_APP(2, 4) KVR_APP(2, 8) KVR_APP(4, 2) KVR_APP(4, 4) KVR_APP(4, 8) KVR_APP(8, 2) KVR_APP(8, 4) KVR_APP(8, 8)
+#undef KVR_APP
+    return check_launch();
+  }
+  append_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, s>>>(*a, lengths, advance);
+  return check_launch();
 }
 
 }  // namespace kvr
@@ -716,9 +809,7 @@ extern "C" int kvr_append(const kvr_append_args* a, kvr_stream_t stream) {
   if (a->bh == 0 || a->n == 0) return KVR_OK;
   if (!a->k || !a->v || !a->key_residual || !a->value_payload || !a->value_scale || !a->value_offset)
     return KVR_ERR_INVALID_ARGUMENT;
-  const int64_t total = (int64_t)a->bh * a->n;
-  append_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, as_stream(stream)>>>(*a, nullptr);
-  return check_launch();
+  return launch_append(a, nullptr, 0, as_stream(stream));
 }
 
 // ------------------------------------------------ lengths in device memory
@@ -732,7 +823,7 @@ __global__ void advance_lengths_kernel(int* lengths, int n) {
   if (lengths[2] == 0) lengths[0] += n;
 }
 
-extern "C" int kvr_append_lengths(const kvr_append_args* a, int* lengths, kvr_stream_t stream) {
+extern "C" int kvr_append_lengths(const kvr_append_args* a, int* lengths, int advance, kvr_stream_t stream) {
   if (!a || !lengths || a->head_dim <= 0 || a->head_dim > kMaxD || a->value_bits < 2 || a->value_bits > 8 ||
       a->bh < 0 || a->n < 0 || a->res_capacity < 0 || a->seq_capacity < 0)
     return KVR_ERR_INVALID_ARGUMENT;
@@ -740,9 +831,7 @@ extern "C" int kvr_append_lengths(const kvr_append_args* a, int* lengths, kvr_st
   if (a->bh == 0 || a->n == 0) return KVR_OK;
   if (!a->k || !a->v || !a->key_residual || !a->value_payload || !a->value_scale || !a->value_offset)
     return KVR_ERR_INVALID_ARGUMENT;
-  const int64_t total = (int64_t)a->bh * a->n;
-  append_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, as_stream(stream)>>>(*a, lengths);
-  return check_launch();
+  return launch_append(a, lengths, advance, as_stream(stream));
 }
 
 extern "C" int kvr_set_lengths(int* lengths, int seq_len, int prefix_len, kvr_stream_t stream) {

@@ -4,10 +4,11 @@ A speculative-decoding round runs a few draft steps; each step appends the
 new token's key/value to every layer of the packed cache and decodes over it
 (packed_review.py:23-31 + :76-78, one launch each per layer and step in the
 reference).  ``DraftLoop`` records ``steps`` such steps for all layers of a
-``PackedKVCache`` in one CUDA graph: per layer and step an append, an
-advance of the layer's device-side length and a decode, all reading the
-lengths from device memory, so the same graph replays at any length the
-capacity allows.  Queries and new keys/values are read from (and outputs
+``PackedKVCache`` in one CUDA graph: per layer and step an append that
+also advances the layer's device-side length, and a decode, both reading
+the lengths from device memory, so the same graph replays at any length the
+capacity allows (the append moves the length on itself once every block
+has written).  Queries and new keys/values are read from (and outputs
 written to) the loop's static buffers ``q``, ``k``, ``v``, ``out``.
 
 Host-side ``commit`` / ``crop`` between rounds keep the device lengths in
@@ -95,8 +96,7 @@ class DraftLoop:
     def _issue(work: List, stream: int) -> None:
         lib = _lib.load()
         for a, dl, launch, res_cap in work:
-            _lib.check("kvr_append_lengths", lib.kvr_append_lengths(a, dl, stream))
-            _lib.check("kvr_advance_lengths", lib.kvr_advance_lengths(dl, 1, stream))
+            _lib.check("kvr_append_lengths", lib.kvr_append_lengths(a, dl, 1, stream))
             _lib.check("kvr_decode_attention_lengths",
                        lib.kvr_decode_attention_lengths(launch.args, dl, res_cap, stream))
 

@@ -202,11 +202,11 @@ class PackedKVCacheLayer:
 
     # ------------------------------------------------- device-side lengths
     def device_lengths(self) -> torch.Tensor:
-        """int32[3] on the device: (sequence length, prefix length, error
-        flag), kept equal to the host lengths by every host-side operation;
+        """int32[4] on the device: (sequence length, prefix length, error
+        flag, scratch), kept equal to the host lengths by every host-side operation;
         the graph-replayable append / advance / decode read and move it."""
         if self._dev_len is None:
-            self._dev_len = torch.zeros(3, dtype=torch.int32, device=self.device)
+            self._dev_len = torch.zeros(4, dtype=torch.int32, device=self.device)
             self._sync_lengths()
         return self._dev_len
 
