@@ -15,9 +15,9 @@ Mirrors kv_reduce/experiments/packed_review.py:17-80:
   reference builds first and packs afterwards never exists.
 * ``install(model)`` patches every decoder layer's attention (:65-80): with
   a ``PackedDraftCache`` and a one-token step, it projects q/k/v, applies the
-  rotary embedding, appends k/v to the packed layer and runs the fused
-  decode kernel over the packed cache; any other call goes to the original
-  forward.
+  rotary embedding and runs ``decode_step`` on the packed layer (append
+  in place + fused decode, two library calls from device-side lengths); any
+  other call goes to the original forward.
 
 Written against the Qwen2 attention module of transformers 5.x (q/k/v/o
 projections, ``head_dim``, ``layer_idx``, rotary ``position_embeddings``).
@@ -31,7 +31,6 @@ import torch
 from transformers.cache_utils import DynamicCache, DynamicLayer
 from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
 
-from .packed_kv_attention import packed_kv_decode_attention
 from .streaming import PackedKVCacheLayer, PackedLayer
 
 
@@ -134,8 +133,7 @@ def install(model, *, split_tokens: int = 0) -> None:
             v = self.v_proj(hidden_states).view(view).transpose(1, 2)
             q, k = apply_rotary_pos_emb(q, k, *position_embeddings)
             packed = past_key_values.layers[self.layer_idx].packed
-            packed.append(k, v)
-            out = packed_kv_decode_attention(q.contiguous(), packed.k, packed.v, split_tokens=split_tokens)
+            out = packed.decode_step(q, k, v, split_tokens=split_tokens)
             return self.o_proj(out.transpose(1, 2).reshape(*shape, -1).contiguous()), None
 
         attn.forward = types.MethodType(forward, attn)

@@ -242,6 +242,74 @@ class PackedKVCacheLayer:
                   out_dtype: torch.dtype | None = None) -> torch.Tensor:
         return packed_kv_decode_attention(query, self.k, self.v, split_tokens=split_tokens, out_dtype=out_dtype)
 
+    def decode_step(self, query: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, split_tokens: int = 0,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        """append(k, v) then attention(query) as two library calls.
+
+        Both read the lengths from the layer's device-side copy and the
+        append moves it on itself, so the host only rewrites the query,
+        new-token and output pointers of argument blocks prepared once per
+        buffer layout (and the calls can be captured in a CUDA graph).  The
+        decode is planned for the buffers' capacity.  The residual buffer is
+        pinned (commit copies the live rows back) so the prepared addresses
+        hold across commits.
+        """
+        n = int(k.shape[2]) if k.dim() == 4 else -1
+        if (k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or k.shape != v.shape or n < 1
+                or tuple(k.shape[:2]) != (self.batch, self.kv_heads) or k.shape[3] != self.head_dim):
+            raise ValueError(f"k/v must be bf16 [{self.batch}, {self.kv_heads}, n, {self.head_dim}].")
+        if (query.dim() != 4 or query.dtype != torch.bfloat16 or query.shape[0] != self.batch
+                or query.shape[2] != 1 or query.shape[3] != self.head_dim or query.shape[1] % self.kv_heads):
+            raise ValueError(f"query must be bf16 [{self.batch}, q_heads, 1, {self.head_dim}].")
+        _lib.require_cuda(query, k, v)
+        if self.seq_len + n > self.capacity or self.residual_len + n > self.cap_residual:
+            self._grow(self.seq_len + n, self.residual_len + n)
+        if self.seq_len == 0:
+            raise ValueError("decode_step needs a prefilled layer.")
+        self.pin_residual = True
+        k, v, query = k.contiguous(), v.contiguous(), query.contiguous()
+        if out is None:
+            out = torch.empty_like(query)
+        stream = self._stream()
+        key = (int(query.shape[1]), int(split_tokens), stream, self.key_payload.data_ptr(),
+               self.key_residual[self._cur].data_ptr(), self.capacity)
+        prep = getattr(self, "_step_prep", None)
+        if prep is None or prep[0] != key:
+            prep = (key,) + self._prepare_step(int(query.shape[1]), int(split_tokens), stream, query, out)
+            self._step_prep = prep
+        _, app, launch = prep
+        app.k, app.v, app.n = k.data_ptr(), v.data_ptr(), n
+        launch.layers[0].query, launch.layers[0].out = query.data_ptr(), out.data_ptr()
+        dl = self.device_lengths().data_ptr()
+        lib = _lib.load()
+        _lib.check("kvr_append_lengths", lib.kvr_append_lengths(app, dl, 1, stream))
+        _lib.check("kvr_decode_attention_lengths",
+                   lib.kvr_decode_attention_lengths(launch.args, dl, self.cap_residual, stream))
+        self.seq_len += n
+        return out
+
+    def _prepare_step(self, q_heads: int, split_tokens: int, stream: int, query: torch.Tensor,
+                      out: torch.Tensor):
+        from .packed_kv_attention import CacheGeometry, DecodeLaunch
+
+        res = self.key_residual[self._cur]
+        a = _lib.AppendArgs()
+        a.key_residual, a.key_residual_bh_stride = res.data_ptr(), res.stride(1)
+        a.value_payload, a.value_payload_bh_stride = self.value_payload.data_ptr(), self.value_payload.stride(1)
+        a.value_scale, a.value_offset = self.value_scale.data_ptr(), self.value_offset.data_ptr()
+        a.value_meta_bh_stride = self.value_scale.stride(1)
+        a.bh, a.seq_len, a.res_len = self.batch * self.kv_heads, 0, 0
+        a.res_capacity, a.seq_capacity = self.cap_residual, self.capacity
+        a.head_dim, a.value_bits = self.head_dim, self.v_bits
+        geom = CacheGeometry(self.batch, q_heads, self.kv_heads, self.head_dim, self.capacity, self.cap_prefix,
+                             self.group_size, self.k_bits, self.v_bits, self.key_payload.stride(1),
+                             self.key_scale.stride(1), res.stride(1), self.value_payload.stride(1),
+                             self.value_scale.stride(1))
+        ptrs = _lib.LayerPtrs(self.key_payload.data_ptr(), self.key_scale.data_ptr(), self.key_offset.data_ptr(),
+                              res.data_ptr(), self.value_payload.data_ptr(), self.value_scale.data_ptr(),
+                              self.value_offset.data_ptr(), query.data_ptr(), out.data_ptr())
+        return a, DecodeLaunch(geom, [ptrs], self.device, split_tokens=split_tokens, stream=stream)
+
     def breakdown(self) -> Dict[str, int]:
         """Byte accounting with the keys of packed_review.py:50-54."""
         k, v = self.k, self.v

@@ -91,3 +91,25 @@ def test_capacity_is_checked_before_replay(kvr):
     with pytest.raises(ValueError):
         loop.replay()
     assert loop.errors() == 0
+
+
+def test_decode_step_matches_append_then_attention(kvr):
+    """PackedKVCacheLayer.decode_step (two library calls from device-side
+    lengths) == append + packed_kv_decode_attention: same cache bytes,
+    outputs within bf16 rounding; across a commit and a capacity growth."""
+    a_cache, b_cache = make_cache(kvr, seed=3, capacity=768), make_cache(kvr, seed=3, capacity=768)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    for step in range(90):   # 700 + 90 > 768: the buffers grow on the way
+        for la, lb in zip(a_cache.layers, b_cache.layers):
+            q = torch.randn(B, HQ, 1, D, generator=g, device="cuda").to(torch.bfloat16)
+            k = torch.randn(B, H, 1, D, generator=g, device="cuda").to(torch.bfloat16)
+            v = torch.randn(B, H, 1, D, generator=g, device="cuda").to(torch.bfloat16)
+            got = la.decode_step(q, k, v)
+            lb.append(k, v)
+            close(got, kvr.packed_kv_decode_attention(q, lb.k, lb.v))
+        if step % 40 == 39:
+            a_cache.commit()
+            b_cache.commit()
+    same_cache(a_cache, b_cache)
+    with pytest.raises(ValueError):
+        a_cache.layers[0].decode_step(q[:, :, :, :64], k, v)
