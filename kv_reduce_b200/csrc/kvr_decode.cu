@@ -34,6 +34,8 @@
 //           counters reset by the merging CTA for the next launch.
 #include "kvr_common.cuh"
 
+#include <type_traits>
+
 #include <algorithm>
 #include <cmath>
 
@@ -527,174 +529,190 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
       const uint32_t st_s = ring_s + stage * C::STAGE;
       const uint16_t* meta0 = reinterpret_cast<const uint16_t*>(st + C::M_OFF);
 
-      // ------------------------------------------------------------ Q K^T
-      float sc[2][4];
-      const bool fast = (n_valid == kChunk) && (tok0 + kChunk <= P) && (log2G >= 5);
-      if (fast) {
-        // whole chunk in one key group: both m-tiles, four independent mma chains
-        // the hi chains start from the zero-point bias
-        float bf[4];
-        group_bias<D>(bf, qs, meta0, lane, dbase);
-        uint32_t kw[4][C::NWK];
+      // A full prefix chunk inside one key group (the common case) runs a
+      // body free of row bounds logic; other chunks take the general body.
+      auto chunk_body = [&](auto full_c) {
+        constexpr bool FULL = decltype(full_c)::value;
+        // ------------------------------------------------------------ Q K^T
+        float sc[2][4];
+        if constexpr (FULL) {
+          // whole chunk in one key group: both m-tiles, four independent mma chains
+          // the hi chains start from the zero-point bias
+          float bf[4];
+          group_bias<D>(bf, qs, meta0, lane, dbase);
+          uint32_t kw[4][C::NWK];
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) load_key_row<D, KB>(kw[rr], st + C::K_OFF, g + 8 * rr, t4);
+          for (int rr = 0; rr < 4; ++rr) load_key_row<D, KB>(kw[rr], st + C::K_OFF, g + 8 * rr, t4);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) bf[k] *= kKeyScale;
-        float h0[4] = {bf[0], bf[1], bf[2], bf[3]}, l0[4] = {0.f, 0.f, 0.f, 0.f};
-        float h1[4] = {bf[0], bf[1], bf[2], bf[3]}, l1[4] = {0.f, 0.f, 0.f, 0.f};
-        qk_chunk<D, KB>(h0, l0, h1, l1, kw, qs, meta0, lane, dbase);
+          for (int k = 0; k < 4; ++k) bf[k] *= kKeyScale;
+          float h0[4] = {bf[0], bf[1], bf[2], bf[3]}, l0[4] = {0.f, 0.f, 0.f, 0.f};
+          float h1[4] = {bf[0], bf[1], bf[2], bf[3]}, l1[4] = {0.f, 0.f, 0.f, 0.f};
+          qk_chunk<D, KB>(h0, l0, h1, l1, kw, qs, meta0, lane, dbase);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          sc[0][k] = (h0[k] + l0[k]) * cs_k;
-          sc[1][k] = (h1[k] + l1[k]) * cs_k;
+          for (int k = 0; k < 4; ++k) {
+            sc[0][k] = (h0[k] + l0[k]) * cs_k;
+            sc[1][k] = (h1[k] + l1[k]) * cs_k;
+          }
+        } else {
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            const int mtok = tok0 + 16 * mt;
+            sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = NEG_INF;
+            if (16 * mt >= n_valid) continue;
+            if (mtok < P) {
+              const int grp = mtok >> log2G;
+              const int slot = (mt == 1 && grp != (tok0 >> log2G)) ? 1 : 0;
+              GroupQ<D> gq;
+              group_query<D, KB>(gq, qs, meta0 + slot * (C::META / 2), lane, dbase);
+              uint32_t kw0[C::NWK], kw1[C::NWK];
+              load_key_row<D, KB>(kw0, st + C::K_OFF, 16 * mt + g, t4);
+              load_key_row<D, KB>(kw1, st + C::K_OFF, 16 * mt + g + 8, t4);
+              const float b0 = gq.bias[0] * kKeyScale, b1 = gq.bias[1] * kKeyScale;
+              float hi[4] = {b0, b1, b0, b1}, lo[4] = {0.f, 0.f, 0.f, 0.f};
+              qk_prefix<D, KB>(hi, lo, kw0, kw1, gq);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) sc[mt][k] = (hi[k] + lo[k]) * cs_k;
+            } else {
+              // BF16 residual window: raw keys x raw query, bf16 mma.
+              uint32_t kr[2][D / 8];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int tok = mtok + g + 8 * h;
+                if (tok < t_end) {
+                  const uint4* src = reinterpret_cast<const uint4*>(kres + (int64_t)(tok - P) * D + dbase);
+#pragma unroll
+                  for (int v = 0; v < D / 32; ++v) {
+                    const uint4 x = __ldg(src + v);
+                    kr[h][4 * v + 0] = x.x; kr[h][4 * v + 1] = x.y; kr[h][4 * v + 2] = x.z; kr[h][4 * v + 3] = x.w;
+                  }
+                } else {
+#pragma unroll
+                  for (int v = 0; v < D / 8; ++v) kr[h][v] = 0u;
+                }
+              }
+              uint32_t qb[D / 8];
+#pragma unroll
+              for (int v = 0; v < D / 32; ++v) {
+                const uint4 x = qs[(D / 32 + v) * 32 + lane];
+                qb[4 * v + 0] = x.x; qb[4 * v + 1] = x.y; qb[4 * v + 2] = x.z; qb[4 * v + 3] = x.w;
+              }
+              float a4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+              for (int js = 0; js < C::KS; ++js)
+                mma_bf16(a4, kr[0][2 * js], kr[1][2 * js], kr[0][2 * js + 1], kr[1][2 * js + 1], qb[2 * js],
+                         qb[2 * js + 1]);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) sc[mt][k] = a4[k] * cs;
+            }
+            if (mtok + g >= t_end) { sc[mt][0] = NEG_INF; sc[mt][1] = NEG_INF; }
+            if (mtok + g + 8 >= t_end) { sc[mt][2] = NEG_INF; sc[mt][3] = NEG_INF; }
+          }
         }
-      } else {
+
+        // ------------------------------------------------------------ softmax
+        float cmax[2];
+        cmax[0] = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
+        cmax[1] = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+        // The running maxima can only move if some lane's own rows exceed
+        // them; otherwise the reduced maxima would not either, so the
+        // reduction and the rescale are skipped (bit-identical either way).
+        const bool grow = (cmax[0] > m_run[0]) || (cmax[1] > m_run[1]);
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            cmax[0] = fmaxf(cmax[0], __shfl_xor_sync(0xffffffffu, cmax[0], o));
+            cmax[1] = fmaxf(cmax[1], __shfl_xor_sync(0xffffffffu, cmax[1], o));
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float mn = fmaxf(m_run[e], cmax[e]);
+            const float alpha = (mn == NEG_INF) ? 1.f : fast_exp2(m_run[e] - mn);
+            m_run[e] = mn;
+            l_run[e] *= alpha;
+            z_run[e] *= alpha;
+#pragma unroll
+            for (int mi = 0; mi < C::KS; ++mi) {
+              acc[mi][e] *= alpha;
+              acc[mi][2 + e] *= alpha;
+            }
+          }
+        }
+        uint32_t pb[2][2];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
-          const int mtok = tok0 + 16 * mt;
-          sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = NEG_INF;
-          if (16 * mt >= n_valid) continue;
-          if (mtok < P) {
-            const int grp = mtok >> log2G;
-            const int slot = (mt == 1 && grp != (tok0 >> log2G)) ? 1 : 0;
-            GroupQ<D> gq;
-            group_query<D, KB>(gq, qs, meta0 + slot * (C::META / 2), lane, dbase);
-            uint32_t kw0[C::NWK], kw1[C::NWK];
-            load_key_row<D, KB>(kw0, st + C::K_OFF, 16 * mt + g, t4);
-            load_key_row<D, KB>(kw1, st + C::K_OFF, 16 * mt + g + 8, t4);
-            const float b0 = gq.bias[0] * kKeyScale, b1 = gq.bias[1] * kKeyScale;
-            float hi[4] = {b0, b1, b0, b1}, lo[4] = {0.f, 0.f, 0.f, 0.f};
-            qk_prefix<D, KB>(hi, lo, kw0, kw1, gq);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) sc[mt][k] = (hi[k] + lo[k]) * cs_k;
+          // token scale s and centred offset z + 2^(vb-1) s of rows g, g+8
+          uint32_t w_lo, w_hi;
+          if (p.vm_staged) {
+            const uint16_t* vm = reinterpret_cast<const uint16_t*>(st + C::VM_OFF);
+            const int r = 16 * mt + g;
+            if constexpr (FULL) {
+              w_lo = (uint32_t)vm[r] | ((uint32_t)vm[kChunk + r] << 16);
+              w_hi = (uint32_t)vm[r + 8] | ((uint32_t)vm[kChunk + r + 8] << 16);
+            } else {
+              // rows [0, n_vm) were copied; the ragged tail [n_vm, n_valid) is
+              // read from global memory; rows past the end contribute zero
+              const int n_vm = n_valid & ~7;
+              auto vmeta = [&](int rr) -> uint32_t {
+                if (rr < n_vm) return (uint32_t)vm[rr] | ((uint32_t)vm[kChunk + rr] << 16);
+                if (rr < n_valid) return (uint32_t)__ldg(vsc + tok0 + rr) | ((uint32_t)__ldg(vof + tok0 + rr) << 16);
+                return 0u;
+              };
+              w_lo = vmeta(r);
+              w_hi = vmeta(r + 8);
+            }
           } else {
-            // BF16 residual window: raw keys x raw query, bf16 mma.
-            uint32_t kr[2][D / 8];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int tok = mtok + g + 8 * h;
-              if (tok < t_end) {
-                const uint4* src = reinterpret_cast<const uint4*>(kres + (int64_t)(tok - P) * D + dbase);
-#pragma unroll
-                for (int v = 0; v < D / 32; ++v) {
-                  const uint4 x = __ldg(src + v);
-                  kr[h][4 * v + 0] = x.x; kr[h][4 * v + 1] = x.y; kr[h][4 * v + 2] = x.z; kr[h][4 * v + 3] = x.w;
-                }
-              } else {
-#pragma unroll
-                for (int v = 0; v < D / 8; ++v) kr[h][v] = 0u;
-              }
-            }
-            uint32_t qb[D / 8];
-#pragma unroll
-            for (int v = 0; v < D / 32; ++v) {
-              const uint4 x = qs[(D / 32 + v) * 32 + lane];
-              qb[4 * v + 0] = x.x; qb[4 * v + 1] = x.y; qb[4 * v + 2] = x.z; qb[4 * v + 3] = x.w;
-            }
-            float a4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int js = 0; js < C::KS; ++js)
-              mma_bf16(a4, kr[0][2 * js], kr[1][2 * js], kr[0][2 * js + 1], kr[1][2 * js + 1], qb[2 * js],
-                       qb[2 * js + 1]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) sc[mt][k] = a4[k] * cs;
+            w_lo = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g);
+            w_hi = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g + 8);
           }
-          if (mtok + g >= t_end) { sc[mt][0] = NEG_INF; sc[mt][1] = NEG_INF; }
-          if (mtok + g + 8 >= t_end) { sc[mt][2] = NEG_INF; sc[mt][3] = NEG_INF; }
+          const float s_lo = bf16lo(w_lo), s_hi = bf16lo(w_hi);
+          const float z_lo = fmaf(s_lo, (float)(1 << (VB - 1)), bf16hi(w_lo));
+          const float z_hi = fmaf(s_hi, (float)(1 << (VB - 1)), bf16hi(w_hi));
+          float pr[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) pr[k] = fast_exp2(sc[mt][k] - m_run[k & 1]);   // -inf -> 0
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            l_run[e] += pr[e] + pr[2 + e];
+            z_run[e] = fmaf(pr[e], z_lo, fmaf(pr[2 + e], z_hi, z_run[e]));
+          }
+          pb[mt][0] = movmatrix_trans(pack_half2(pr[0] * s_lo, pr[1] * s_lo));
+          pb[mt][1] = movmatrix_trans(pack_half2(pr[2] * s_hi, pr[3] * s_hi));
         }
-      }
 
-      // ------------------------------------------------------------ softmax
-      float cmax[2];
-      cmax[0] = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
-      cmax[1] = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+        // ---------------------------------------------------------------- P V
 #pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        cmax[0] = fmaxf(cmax[0], __shfl_xor_sync(0xffffffffu, cmax[0], o));
-        cmax[1] = fmaxf(cmax[1], __shfl_xor_sync(0xffffffffu, cmax[1], o));
-      }
-      const bool grow = (cmax[0] > m_run[0]) || (cmax[1] > m_run[1]);
-      if (__any_sync(0xffffffffu, grow)) {
+        for (int ks = 0; ks < 2; ++ks) {
+          if constexpr (!FULL) {
+            if (16 * ks >= n_valid) break;
+          }
+          uint32_t vx[2][C::CRV];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float mn = fmaxf(m_run[e], cmax[e]);
-          const float alpha = (mn == NEG_INF) ? 1.f : fast_exp2(m_run[e] - mn);
-          m_run[e] = mn;
-          l_run[e] *= alpha;
-          z_run[e] *= alpha;
+          for (int q4 = 0; q4 < C::CRV / 2; ++q4) {
+            const int m = 4 * q4 + (lane >> 3);
+            const int blk = m / C::CRV, c16 = m % C::CRV;
+            const int row = 16 * ks + 8 * blk + (lane & 7);
+            const uint32_t addr = st_s + C::V_OFF + row * C::RBV + 16 * (c16 ^ swz<C::CRV>(row));
+            uint32_t r0, r1, r2, r3;
+            ldsm_x4_trans(addr, r0, r1, r2, r3);
+            const int mb = 4 * q4;
+            vx[(mb + 0) / C::CRV][(mb + 0) % C::CRV] = r0;
+            vx[(mb + 1) / C::CRV][(mb + 1) % C::CRV] = r1;
+            vx[(mb + 2) / C::CRV][(mb + 2) % C::CRV] = r2;
+            vx[(mb + 3) / C::CRV][(mb + 3) % C::CRV] = r3;
+          }
 #pragma unroll
           for (int mi = 0; mi < C::KS; ++mi) {
-            acc[mi][e] *= alpha;
-            acc[mi][2 + e] *= alpha;
+            const int ra = 2 * mi, rb = 2 * mi + 1;
+            const uint32_t a0 = codes_to_h2<VB, true>(vx[0][ra / C::CPB_V], ra % C::CPB_V);
+            const uint32_t a1 = codes_to_h2<VB, true>(vx[0][rb / C::CPB_V], rb % C::CPB_V);
+            const uint32_t a2 = codes_to_h2<VB, true>(vx[1][ra / C::CPB_V], ra % C::CPB_V);
+            const uint32_t a3 = codes_to_h2<VB, true>(vx[1][rb / C::CPB_V], rb % C::CPB_V);
+            mma_f16(acc[mi], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
           }
         }
-      }
-      uint32_t pb[2][2];
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        // token scale s and centred offset z + 2^(vb-1) s of rows g, g+8
-        uint32_t w_lo, w_hi;
-        if (p.vm_staged) {
-          // rows [0, n_vm) were copied; the ragged tail [n_vm, n_valid) is
-          // read from global memory; rows past the end contribute zero
-          const uint16_t* vm = reinterpret_cast<const uint16_t*>(st + C::VM_OFF);
-          const int n_vm = n_valid & ~7;
-          auto vmeta = [&](int r) -> uint32_t {
-            if (r < n_vm) return (uint32_t)vm[r] | ((uint32_t)vm[kChunk + r] << 16);
-            if (r < n_valid) return (uint32_t)__ldg(vsc + tok0 + r) | ((uint32_t)__ldg(vof + tok0 + r) << 16);
-            return 0u;
-          };
-          const int r = 16 * mt + g;
-          w_lo = vmeta(r);
-          w_hi = vmeta(r + 8);
-        } else {
-          w_lo = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g);
-          w_hi = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g + 8);
-        }
-        const float s_lo = bf16lo(w_lo), s_hi = bf16lo(w_hi);
-        const float z_lo = fmaf(s_lo, (float)(1 << (VB - 1)), bf16hi(w_lo));
-        const float z_hi = fmaf(s_hi, (float)(1 << (VB - 1)), bf16hi(w_hi));
-        float pr[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) pr[k] = fast_exp2(sc[mt][k] - m_run[k & 1]);   // -inf -> 0
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          l_run[e] += pr[e] + pr[2 + e];
-          z_run[e] = fmaf(pr[e], z_lo, fmaf(pr[2 + e], z_hi, z_run[e]));
-        }
-        pb[mt][0] = movmatrix_trans(pack_half2(pr[0] * s_lo, pr[1] * s_lo));
-        pb[mt][1] = movmatrix_trans(pack_half2(pr[2] * s_hi, pr[3] * s_hi));
-      }
-
-      // ---------------------------------------------------------------- P V
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        if (16 * ks >= n_valid) break;
-        uint32_t vx[2][C::CRV];
-#pragma unroll
-        for (int q4 = 0; q4 < C::CRV / 2; ++q4) {
-          const int m = 4 * q4 + (lane >> 3);
-          const int blk = m / C::CRV, c16 = m % C::CRV;
-          const int row = 16 * ks + 8 * blk + (lane & 7);
-          const uint32_t addr = st_s + C::V_OFF + row * C::RBV + 16 * (c16 ^ swz<C::CRV>(row));
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4_trans(addr, r0, r1, r2, r3);
-          const int mb = 4 * q4;
-          vx[(mb + 0) / C::CRV][(mb + 0) % C::CRV] = r0;
-          vx[(mb + 1) / C::CRV][(mb + 1) % C::CRV] = r1;
-          vx[(mb + 2) / C::CRV][(mb + 2) % C::CRV] = r2;
-          vx[(mb + 3) / C::CRV][(mb + 3) % C::CRV] = r3;
-        }
-#pragma unroll
-        for (int mi = 0; mi < C::KS; ++mi) {
-          const int ra = 2 * mi, rb = 2 * mi + 1;
-          const uint32_t a0 = codes_to_h2<VB, true>(vx[0][ra / C::CPB_V], ra % C::CPB_V);
-          const uint32_t a1 = codes_to_h2<VB, true>(vx[0][rb / C::CPB_V], rb % C::CPB_V);
-          const uint32_t a2 = codes_to_h2<VB, true>(vx[1][ra / C::CPB_V], ra % C::CPB_V);
-          const uint32_t a3 = codes_to_h2<VB, true>(vx[1][rb / C::CPB_V], rb % C::CPB_V);
-          mma_f16(acc[mi], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
-        }
-      }
+      };
+      if ((n_valid == kChunk) && (tok0 + kChunk <= P) && (log2G >= 5)) chunk_body(std::true_type{});
+      else chunk_body(std::false_type{});
       __syncwarp();
       stage = stage + 1 == kStages ? 0 : stage + 1;
     }
