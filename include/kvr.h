@@ -238,6 +238,17 @@ int kvr_decode_attention_noalloc(const kvr_decode_args* a, kvr_stream_t stream);
 int kvr_decode_attention_lengths(const kvr_decode_args* a, const int* lengths, int residual_capacity,
                                  kvr_stream_t stream);
 
+/* The same decode on the CUDA cores (fp32 FMA, no tensor cores): the
+ * measured A/B baseline the tensor-core kernel is adopted against.  Same
+ * arguments; a->workspace must hold kvr_decode_simt_workspace(a) bytes
+ * (split partials; counters unused; 0 = invalid or unsupported).
+ * Supported: (D, key bits, value bits, HQ/HKV) in {(128,4,4,6), (128,2,2,6),
+ * (128,4,4,4), (64,8,4,4), (64,4,8,4)}, group_size a power of two >= 32.
+ * No reference counterpart (the reference's Triton kernels are the
+ * CUDA-core formulation).                                                  */
+size_t kvr_decode_simt_workspace(const kvr_decode_args* a);
+int kvr_decode_attention_simt(const kvr_decode_args* a, kvr_stream_t stream);
+
 /* LSE merge of externally produced partials (the cross-GPU token split):
  * parts: n_parts blocks of [rows] (m, l) pairs and [rows, D] unnormalised
  * outputs, m in log2 units; out[rows, D] bf16 = sum_p 2^(m_p-M) o_p /

@@ -39,6 +39,8 @@ EXPORTED_SYMBOLS = (
     "kvr_flush_groups",
     "kvr_decode_plan",
     "kvr_decode_attention",
+    "kvr_decode_attention_simt",
+    "kvr_decode_simt_workspace",
     "kvr_lse_merge",
     "kvr_decode_partial",
     "kvr_decode_attention_noalloc",
@@ -178,6 +180,8 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_partial.argtypes = [POINTER(DecodeArgs), c_int, c_int, c_void_p, c_void_p, c_void_p]
     lib.kvr_lse_merge.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     lib.kvr_decode_attention_noalloc.argtypes = [POINTER(DecodeArgs), c_void_p]
+    lib.kvr_decode_attention_simt.argtypes = [POINTER(DecodeArgs), c_void_p]
+    lib.kvr_decode_simt_workspace.argtypes = [POINTER(DecodeArgs)]
     lib.kvr_append_lengths.argtypes = [POINTER(AppendArgs), c_void_p, c_int, c_void_p]
     lib.kvr_advance_lengths.argtypes = [c_void_p, c_int, c_void_p]
     lib.kvr_set_lengths.argtypes = [c_void_p, c_int, c_int, c_void_p]
@@ -190,6 +194,7 @@ def load() -> ctypes.CDLL:
     for name in EXPORTED_SYMBOLS:
         if name not in ("kvr_version", "kvr_status_string", "kvr_last_error"):
             getattr(lib, name).restype = c_int
+    lib.kvr_decode_simt_workspace.restype = c_size_t
     _lib = lib
     return lib
 

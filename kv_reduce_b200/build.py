@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libkvr.so"
-SOURCES = ["kvr_capi.cu", "kvr_pack.cu", "kvr_decode.cu", "kvr_exchange.cu"]
+SOURCES = ["kvr_capi.cu", "kvr_pack.cu", "kvr_decode.cu", "kvr_decode_simt.cu", "kvr_exchange.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

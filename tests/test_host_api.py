@@ -14,7 +14,7 @@ def test_library_exports_header_symbols(built_lib):
     from kv_reduce_b200 import _lib
 
     header = (ROOT / "include" / "kvr.h").read_text()
-    declared = set(re.findall(r"^(?:int|const char\*)\s+(kvr_\w+)\(", header, flags=re.M))
+    declared = set(re.findall(r"^(?:int|size_t|const char\*)\s+(kvr_\w+)\(", header, flags=re.M))
     assert declared == set(_lib.EXPORTED_SYMBOLS)
     lib = _lib.load()
     for name in declared:
