@@ -48,6 +48,7 @@ constexpr int kStages = 2;    // cp.async ring depth per warp (one chunk ahead h
 constexpr int kHeads = 8;     // N of the mma = padded GQA group
 constexpr int kMaxSplits = 256;
 constexpr int kFan = 16;      // partials merged per merge step
+static_assert(kFan <= 16, "a cluster of kFan CTAs must be launchable");
 constexpr uint32_t kMagic = 0x64006400u;  // fp16x2 {1024, 1024}
 
 template <int D, int KB, int VB>
@@ -73,8 +74,11 @@ struct Cfg {
   static constexpr int QS_OFF = kWarps * RING;
   static constexpr int QS_BYTES = (D / 16) * 32 * 16;
   static constexpr int MERGE = kWarps * kHeads * (D + 2) * 4;
+  // cluster merge: this CTA's partial (M[8], L[8], o[8][D]) after the warp merge area
+  static constexpr int CPART_OFF = (MERGE + 15) / 16 * 16;
+  static constexpr int CPART_END = CPART_OFF + kHeads * (D + 2) * 4;
   static constexpr int BODY = QS_OFF + QS_BYTES;
-  static constexpr int SMEM = BODY > MERGE ? BODY : MERGE;
+  static constexpr int SMEM = BODY > CPART_END ? BODY : CPART_END;
   // resident CTAs per SM the register budget is sized for: 4 (16 warps) unless
   // 8-bit keys at D=128 need the registers of a 3-CTA budget
   static constexpr int MIN_CTAS = (KB == 8 && D == 128) ? 3 : 4;
@@ -120,7 +124,36 @@ struct Params {
   float* out_o;                  // partial mode: unnormalised o
   const int* dev_len;            // non-null: sequence / prefix length read here at run time
   int res_cap;                   // residual rows the key residual buffer holds
+  int cluster;                   // > 1: launched in clusters of NS CTAs, one per unit
 };
+
+// ------------------------------------------------------- thread-block clusters
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t smem_addr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 dsmem_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+  return v;
+}
 
 // ----------------------------------------------------------- register maps
 // Key register r of a thread (head-dim slice [t4*D/4, +D/4)):
@@ -776,7 +809,9 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         }
       }
     };
-    float* my_part = NS > 1 ? p.part1 + ((int64_t)unit * NS + sp) * pstride : nullptr;
+    const bool clustered = NS > 1 && p.cluster > 1;
+    float* cpart = reinterpret_cast<float*>(smem + C::CPART_OFF);
+    float* my_part = NS > 1 ? (clustered ? cpart : p.part1 + ((int64_t)unit * NS + sp) * pstride) : nullptr;
     for (int idx = threadIdx.x; idx < gqa * (D / 4); idx += blockDim.x) {
       const int h = idx / (D / 4), d = 4 * (idx % (D / 4));
       float M = NEG_INF;
@@ -810,7 +845,12 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     // head, lane = 4 consecutive d; every load of a head is issued before
     // the first use, so a merge costs one L2 round trip per head rather
     // than one per partial.
-    auto merge = [&](const float* src, int n, float* dst) {
+    // The loads come from global memory (split partials, src) or, in a
+    // cluster (from_cluster), from the shared memory of the cluster's CTAs:
+    // partial s is CTA s's cpart.  The source is a compile-time choice so
+    // the global merge keeps all its loads in flight before the first use.
+    auto merge = [&](auto from_cluster, const float* src, int n, float* dst) {
+      constexpr bool DSM = decltype(from_cluster)::value;
       for (int h = warp; h < gqa; h += kWarps) {
         const int d = 4 * lane;
         const bool dl = d < D;
@@ -819,10 +859,17 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
 #pragma unroll
         for (int s = 0; s < kFan; ++s) {
           const bool ok = s < n;
-          ms[s] = ok ? __ldcg(src + s * pstride + h) : NEG_INF;
-          ls[s] = ok ? __ldcg(src + s * pstride + kHeads + h) : 0.f;
-          vs[s] = (ok && dl) ? __ldcg(reinterpret_cast<const float4*>(src + s * pstride + 2 * kHeads + h * D + d))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+          if constexpr (DSM) {
+            const uint32_t rs = ok ? dsmem_map(smem_u32(cpart), s) : 0u;
+            ms[s] = ok ? dsmem_f32(rs + 4 * h) : NEG_INF;
+            ls[s] = ok ? dsmem_f32(rs + 4 * (kHeads + h)) : 0.f;
+            vs[s] = (ok && dl) ? dsmem_f32x4(rs + 4 * (2 * kHeads + h * D + d)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          } else {
+            ms[s] = ok ? __ldcg(src + s * pstride + h) : NEG_INF;
+            ls[s] = ok ? __ldcg(src + s * pstride + kHeads + h) : 0.f;
+            vs[s] = (ok && dl) ? __ldcg(reinterpret_cast<const float4*>(src + s * pstride + 2 * kHeads + h * D + d))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
         float M = NEG_INF;
 #pragma unroll
@@ -846,6 +893,16 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         }
       }
     };
+    if (clustered) {
+      // Cluster merge (the cluster is all NS splits of this unit): every
+      // CTA's partial sits in its own shared memory; rank 0 merges them over
+      // distributed shared memory straight into the output.  The second
+      // barrier keeps every CTA's shared memory alive until rank 0 has read it.
+      cluster_sync_all();
+      if (cluster_rank() == 0) merge(std::true_type{}, nullptr, NS, nullptr);
+      cluster_sync_all();
+      continue;
+    }
     const int G1 = p.groups1;
     const int grp1 = sp / kFan;
     const int n1 = min(kFan, NS - grp1 * kFan);
@@ -857,11 +914,11 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     __threadfence();
     const float* src1 = p.part1 + ((int64_t)unit * NS + grp1 * kFan) * pstride;
     if (G1 == 1) {
-      merge(src1, n1, nullptr);
+      merge(std::false_type{}, src1, n1, nullptr);
       if (threadIdx.x == 0) p.cnt1[(int64_t)unit * G1 + grp1] = 0;
       continue;
     }
-    merge(src1, n1, p.part2 + ((int64_t)unit * G1 + grp1) * pstride);
+    merge(std::false_type{}, src1, n1, p.part2 + ((int64_t)unit * G1 + grp1) * pstride);
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -871,7 +928,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     __syncthreads();
     if (!s_flag) continue;
     __threadfence();
-    merge(p.part2 + (int64_t)unit * G1 * pstride, G1, nullptr);
+    merge(std::false_type{}, p.part2 + (int64_t)unit * G1 * pstride, G1, nullptr);
     if (threadIdx.x == 0) p.cnt2[unit] = 0;
   }
 }
@@ -901,7 +958,7 @@ __global__ void lse_merge_kernel(const float* __restrict__ ml, const float* __re
 
 // ------------------------------------------------------------------ host
 struct Plan {
-  int num_splits = 1, chunks_per_split = 1, items = 1, grid = 1, groups1 = 1;
+  int num_splits = 1, chunks_per_split = 1, items = 1, grid = 1, groups1 = 1, cluster = 1;
   size_t counters = 0, part_bytes = 0;
 };
 
@@ -1051,6 +1108,7 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   p.out_o = nullptr;
   p.dev_len = nullptr;
   p.res_cap = a->seq_len - a->prefix_len;
+  p.cluster = pl.cluster;
 }
 
 // Per-device, per-instantiation set-up: dynamic shared memory limit and
@@ -1070,6 +1128,9 @@ static int prepare(int* ctas_per_sm) {
     // persistent grid is sized for is what the SM actually hosts
     e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
+    // clusters of up to 16 CTAs (the cluster merge); refused on parts without them
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      (void)cudaGetLastError();
     int n = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kWarps * 32, C::SMEM);
     if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
@@ -1077,6 +1138,76 @@ static int prepare(int* ctas_per_sm) {
   }
   *ctas_per_sm = occ[dev];
   return KVR_OK;
+}
+
+// Clusters of `cl` CTAs that can be resident at once on this device (0 when
+// the size is unsupported), per device and size.
+template <int D, int KB, int VB, int MAXL>
+static int active_clusters(int cl) {
+  static int cache[64][17];
+  static bool init[64][17];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  dev &= 63;
+  if (cl < 2 || cl > 16) return 0;
+  if (!init[dev][cl]) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(cl);
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = Cfg<D, KB, VB>::SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel<D, KB, VB, MAXL>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    cache[dev][cl] = n;
+    init[dev][cl] = true;
+  }
+  return cache[dev][cl];
+}
+
+// Cluster size for a plan: all splits of a unit in one cluster (at most
+// kFan of them, so the partials are merged in the same order as the global
+// single-level merge and the output is bit-identical to it), only when every
+// CTA takes exactly one item and the device holds every cluster at once.
+// With more splits, clusters of kFan plus a global level measured slower on
+// B200 than two global levels (uneven cluster placement over the GPCs and a
+// costlier launch), so those plans keep the global merge.
+template <int D, int KB, int VB, int MAXL>
+static int cluster_for(const Plan& pl) {
+  const int ns = pl.num_splits;
+  if (ns < 2 || ns > kFan || pl.items > pl.grid) return 1;
+  const int n = active_clusters<D, KB, VB, MAXL>(ns);
+  return (n > 0 && pl.items / ns <= n) ? ns : 1;
+}
+
+template <int D, int KB, int VB, int MAXL>
+static void launch(const Params<MAXL>& p, const Plan& pl, cudaStream_t s) {
+  using C = Cfg<D, KB, VB>;
+  if (pl.cluster <= 1) {
+    decode_kernel<D, KB, VB, MAXL><<<pl.grid, kWarps * 32, C::SMEM, s>>>(p);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pl.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, decode_kernel<D, KB, VB, MAXL>, p);
 }
 
 template <int D, int KB, int VB>
@@ -1098,17 +1229,19 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
   }
   if (dev_st != KVR_OK) return dev_st;
   if (a->n_layers == 1) {
+    pl.cluster = cluster_for<D, KB, VB, 1>(pl);
     Params<1> p;
     fill_params(p, a, pl, tb, te);
     p.out_ml = out_ml; p.out_o = out_o;
     if (dev_len) { p.dev_len = dev_len; p.res_cap = res_cap; }
-    decode_kernel<D, KB, VB, 1><<<pl.grid, kWarps * 32, C::SMEM, s>>>(p);
+    launch<D, KB, VB, 1>(p, pl, s);
   } else {
+    pl.cluster = cluster_for<D, KB, VB, KVR_MAX_LAYERS>(pl);
     Params<KVR_MAX_LAYERS> p;
     fill_params(p, a, pl, tb, te);
     p.out_ml = out_ml; p.out_o = out_o;
     if (dev_len) { p.dev_len = dev_len; p.res_cap = res_cap; }
-    decode_kernel<D, KB, VB, KVR_MAX_LAYERS><<<pl.grid, kWarps * 32, C::SMEM, s>>>(p);
+    launch<D, KB, VB, KVR_MAX_LAYERS>(p, pl, s);
   }
   return check_launch();
 }

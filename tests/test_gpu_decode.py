@@ -160,6 +160,29 @@ def test_multi_layer_launch_equals_per_layer(kvr):
         assert torch.equal(single, o)
 
 
+@pytest.mark.parametrize("split,layers", [(256, 8), (512, 32)])
+def test_cluster_merge_equals_global_merge(kvr, split, layers):
+    """A launch whose CTAs each take one split, with at most 16 splits per
+    (layer, b, kv head), merges them inside a thread-block cluster over
+    distributed shared memory (4096 tokens, batch 4: split 256 -> 16
+    splits, split 512 -> 8).  The same layer repeated in a multi-layer
+    launch has more items than resident CTAs and merges through global
+    memory.  Same partials in the same order, so bit-identical; and within
+    the oracle's tolerance."""
+    from kv_reduce_b200 import workloads
+
+    wl = workloads.CONFIGS["2"].scaled(seq_len=4096, layers=1)
+    k, v = workloads.make_layer_kv(wl, 0, batch=4)
+    q = workloads.make_query(wl, 0, batch=4)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+    single = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=split)
+    many = kvr.packed_kv_decode_attention_layers([q] * layers, [pk] * layers, [pv] * layers, split_tokens=split)
+    for o in many:
+        assert torch.equal(o, single)
+    out32 = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=split, out_dtype=F32)
+    check(out32, oracle_out(k, v, q, 4, 4, 32, 128), f"split {split}")
+
+
 def test_token_shards_merge_to_full(kvr):
     """Partial decode over token shards + LSE merge == full decode (the
     cross-GPU split of one long sequence, emulated on one GPU)."""
