@@ -994,7 +994,17 @@ static Plan make_plan(const kvr_decode_args* a, int tok_begin, int tok_end, int 
       const int64_t items = units * cand;
       const int64_t waves = (items + slots - 1) / slots;
       const double per_item = (double)cps / kWarps + 1.5;
-      const double merge = cand > 1 ? 1.0 + (cand > kFan ? 1.0 : 0.0) : 0.0;
+      // merge cost, in units of one chunk per warp (about 1 us when a launch
+      // is latency-bound).  A plan that fits in one wave merges up to kFan
+      // splits in a thread-block cluster (about 2) and more splits in two
+      // global levels whose cost grows with the second level's fan-in
+      // (5 + groups/4); both fitted to single-layer launches on B200
+      // (e.g. 4K tokens: 16 splits 8.8 us vs 64 splits 11.1 us; 32K: 128
+      // splits 15.1 us vs 256 splits 16.8 us).  Plans of several waves
+      // overlap the merge with other items' work.
+      double merge = cand > 1 ? 1.0 + (cand > kFan ? 1.0 : 0.0) : 0.0;
+      if (cand > 1 && items <= slots)
+        merge = cand <= kFan ? 2.0 : 5.0 + (double)((cand + kFan - 1) / kFan) / 4.0;
       const double t = waves * per_item + merge;
       if (t < best - 1e-9) { best = t; ns = cand; }
     }
