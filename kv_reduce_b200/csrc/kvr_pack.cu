@@ -247,51 +247,87 @@ __device__ __forceinline__ void store_bytes(uint8_t* p, uint64_t w) {
   else *reinterpret_cast<uint2*>(p) = make_uint2((uint32_t)w, (uint32_t)(w >> 32));
 }
 
-// Per-token values: a warp per row, lane l owns channels [l*K, l*K + K);
-// RPW rows per warp iteration keep several row loads in flight.
-template <int K, int BITS, int RPW>
+// Per-token values, 8 lanes per row: lane l serves row (l >> 3) of a 4-row
+// block and owns channels [(l & 7) * KL, +KL), KL = D / 8, loaded with
+// 16-byte loads; the row's min/max takes three shuffles within its 8 lanes,
+// and each lane stores its KL codes as one contiguous KL*BITS/8-byte piece.
+// BPW blocks per warp iteration keep several rows' loads in flight.  Same
+// arithmetic as the reference's per-row rule (exact min/max, IEEE scale,
+// affine_code_rcp), so the codes and metadata are bit-identical to it.
+template <int KL, int BITS, int BPW>
 __global__ void __launch_bounds__(256) quant_token_fast(kvr_token_quant_args a) {
-  constexpr int LB = K * BITS / 8;   // packed bytes per lane
+  constexpr int LB = KL * BITS / 8;   // packed bytes per lane
+  constexpr int NW = (LB + 3) / 4;    // ... as 32-bit words
   constexpr int levels = (1 << BITS) - 1;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, sub = lane & 7, rsel = lane >> 3;
   const int warp0 = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
-  const int bpb = (a.rows + RPW - 1) / RPW;   // row blocks per b*h slab
+  constexpr int RB = 4 * BPW;                 // rows per warp iteration
+  const int bpb = (a.rows + RB - 1) / RB;     // row blocks per b*h slab
   const int nblocks = a.bh * bpb;
+  const int row_bytes = 8 * LB;
   for (int ib = warp0; ib < nblocks; ib += nwarps) {
     const int bh = ib / bpb;
-    const int r0 = (ib - bh * bpb) * RPW;
-    const int nr = min(RPW, a.rows - r0);
-    const uint16_t* x = a.x + (int64_t)bh * a.x_bh_stride + (int64_t)r0 * a.x_row_stride + lane * K;
-    uint8_t* dst = a.payload + (int64_t)bh * a.payload_bh_stride + (int64_t)(a.row0 + r0) * (32 * LB) + lane * LB;
-    const int64_t meta0 = (int64_t)bh * a.meta_bh_stride + a.row0 + r0;
-    float xv[RPW][K];
+    const int rb = (ib - bh * bpb) * RB;
+    float xv[BPW][KL];
+    bool ok[BPW];
 #pragma unroll
-    for (int rr = 0; rr < RPW; ++rr)
-      if (rr < nr) load_bf16x<K>(x + (int64_t)rr * a.x_row_stride, xv[rr]);
+    for (int u = 0; u < BPW; ++u) {
+      const int r = rb + 4 * u + rsel;
+      ok[u] = r < a.rows;
+      if (ok[u]) {
+        const uint16_t* x = a.x + (int64_t)bh * a.x_bh_stride + (int64_t)r * a.x_row_stride + sub * KL;
 #pragma unroll
-    for (int rr = 0; rr < RPW; ++rr) {
-      if (rr >= nr) break;   // warp-uniform
-      float mn = xv[rr][0], mx = xv[rr][0];
+        for (int v = 0; v < KL / 8; ++v) {
+          float t[8];
+          load_bf16x<8>(x + 8 * v, t);
 #pragma unroll
-      for (int k = 1; k < K; ++k) {
-        mn = fminf(mn, xv[rr][k]);
-        mx = fmaxf(mx, xv[rr][k]);
+          for (int k = 0; k < 8; ++k) xv[u][8 * v + k] = t[k];
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < KL; ++k) xv[u][k] = 0.f;   // keeps the group's shuffles defined
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < BPW; ++u) {
+      float mn = xv[u][0], mx = xv[u][0];
+#pragma unroll
+      for (int k = 1; k < KL; ++k) {
+        mn = fminf(mn, xv[u][k]);
+        mx = fmaxf(mx, xv[u][k]);
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
+      for (int o = 4; o > 0; o >>= 1) {   // within the row's 8 lanes
         mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       }
       const float scale = affine_scale(mn, mx, BITS);
       const float inv = __frcp_rn(scale);
-      uint64_t w = 0;
+      uint32_t w[NW];
 #pragma unroll
-      for (int k = 0; k < K; ++k) w |= (uint64_t)affine_code_rcp(xv[rr][k], mn, scale, inv, levels) << (k * BITS);
-      store_bytes<LB>(dst + (int64_t)rr * (32 * LB), w);
-      if (lane == 0) {
-        a.scale[meta0 + rr] = f32_to_bf16_bits(scale);
-        a.offset[meta0 + rr] = f32_to_bf16_bits(mn);
+      for (int i = 0; i < NW; ++i) w[i] = 0u;
+#pragma unroll
+      for (int k = 0; k < KL; ++k)
+        w[(k * BITS) / 32] |= affine_code_rcp(xv[u][k], mn, scale, inv, levels) << ((k * BITS) % 32);
+      if (!ok[u]) continue;
+      const int r = rb + 4 * u + rsel;
+      uint8_t* dst = a.payload + (int64_t)bh * a.payload_bh_stride + (int64_t)(a.row0 + r) * row_bytes + sub * LB;
+      if constexpr (LB == 2) {
+        *reinterpret_cast<uint16_t*>(dst) = (uint16_t)w[0];
+      } else if constexpr (LB == 4) {
+        *reinterpret_cast<uint32_t*>(dst) = w[0];
+      } else if constexpr (LB == 8) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < LB / 16; ++i)
+          reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      }
+      if (sub == 0) {
+        const int64_t m = (int64_t)bh * a.meta_bh_stride + a.row0 + r;
+        a.scale[m] = f32_to_bf16_bits(scale);
+        a.offset[m] = f32_to_bf16_bits(mn);
       }
     }
   }
@@ -705,17 +741,19 @@ extern "C" int kvr_quantize_per_token(const kvr_token_quant_args* a, kvr_stream_
   if (generic && (!a->codes_scratch || a->row0 != 0)) return KVR_ERR_INVALID_ARGUMENT;
   const int64_t total = (int64_t)a->bh * a->rows;
   {
-    const int D = a->head_dim, bits = a->bits, K = D / 32;
+    const int D = a->head_dim, bits = a->bits, KL = D / 8;
     const bool fast = !generic && total < (1ll << 30) && (bits == 2 || bits == 4 || bits == 8) &&
-                      (D == 64 || D == 128 || D == 256) &&
-                      (K * bits) % 8 == 0 && al(a->x, 16) && a->x_bh_stride % K == 0 && a->x_row_stride % K == 0 &&
-                      al(a->payload, 16) && a->payload_bh_stride % 8 == 0;
+                      (D == 64 || D == 128 || D == 256) && al(a->x, 16) && a->x_bh_stride % 8 == 0 &&
+                      a->x_row_stride % 8 == 0 && al(a->payload, 16) && a->payload_bh_stride % 16 == 0;
     if (fast) {
-      constexpr int RPW = 4;
-      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 8 * RPW - 1) / (8 * RPW), 148 * 64));
-#define KVR_TOK(K_, B_) \
-  if (K == K_ && bits == B_) quant_token_fast<K_, B_, RPW><<<grid, 256, 0, as_stream(stream)>>>(*a);
-      KVR_TOK(2, 4) KVR_TOK(2, 8) KVR_TOK(4, 2) KVR_TOK(4, 4) KVR_TOK(4, 8) KVR_TOK(8, 2) KVR_TOK(8, 4) KVR_TOK(8, 8)
+      // warps of 4 rows per block: 2 blocks per iteration, 1 at D=256 (registers)
+      const int bpw = KL == 32 ? 1 : 2;
+      const int64_t warps = (total + 4 * bpw - 1) / (4 * bpw);
+      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, 148 * 64));
+#define KVR_TOK(K_, B_, P_) \
+  if (KL == K_ && bits == B_) quant_token_fast<K_, B_, P_><<<grid, 256, 0, as_stream(stream)>>>(*a);
+      KVR_TOK(8, 2, 2) KVR_TOK(8, 4, 2) KVR_TOK(8, 8, 2) KVR_TOK(16, 2, 2) KVR_TOK(16, 4, 2) KVR_TOK(16, 8, 2)
+      KVR_TOK(32, 2, 1) KVR_TOK(32, 4, 1) KVR_TOK(32, 8, 1)
 #undef KVR_TOK
       return check_launch();
     }
