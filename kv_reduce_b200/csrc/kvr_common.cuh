@@ -31,6 +31,49 @@ inline cudaStream_t as_stream(kvr_stream_t s) { return reinterpret_cast<cudaStre
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ------------------------------------------- programmatic dependent launch
+// The decode and append kernels of a decode loop are launched with
+// programmatic stream serialization (pdl_launch): the next such kernel in the
+// stream may be scheduled while this one still runs.  Each of them calls
+// pdl_wait() before touching global memory: it waits until the previous
+// kernel in the stream has completed and its memory operations are visible
+// -- so the ordering is the stream's, and only the launch latency overlaps.
+// pdl_trigger() lets the next kernel be scheduled: at the start of a short
+// kernel (pdl_enter), after its main loop for a long one, so the next
+// kernel's CTAs are not placed beside a running wave.  A previous kernel that never
+// triggers (any other code's kernel) simply completes first.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+  pdl_trigger();
+  pdl_wait();
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              int cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // ------------------------------------------------------------ bf16 bits
 // bf16 <-> fp32 on raw 16-bit patterns.  bf16 -> fp32 is exact; fp32 ->
 // bf16 rounds to nearest even like torch's Tensor.to(torch.bfloat16).

@@ -538,6 +538,7 @@ __device__ __forceinline__ void advance_after_append(int* lengths, int n) {
 
 __global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args a, int* lengths, int advance) {
   __shared__ uint8_t codes_s[kTokWarps][kMaxD];
+  pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = a.head_dim, bits = a.value_bits;
   if (lengths) {
@@ -604,6 +605,7 @@ __global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args 
 // value channels in registers (as quant_token_fast).
 template <int K, int BITS>
 __global__ void __launch_bounds__(256) append_fast(kvr_append_args a, int* lengths, int advance) {
+  pdl_enter();
   constexpr int LB = K * BITS / 8;
   constexpr int levels = (1 << BITS) - 1;
   const int lane = threadIdx.x & 31;
@@ -681,12 +683,13 @@ static int launch_append(const kvr_append_args* a, int* lengths, int advance, cu
   if (fast) {
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 7) / 8, 148 * 64));
 #define KVR_APP(K_, B_) \
-  if (K == K_ && bits == B_) append_fast<K_, B_><<<grid, 256, 0, s>>>(*a, lengths, advance);
+  if (K == K_ && bits == B_) (void)pdl_launch(append_fast<K_, B_>, dim3(grid), dim3(256), 0, s, 1, *a, lengths, advance);
     KVR_APP(2, 4) KVR_APP(2, 8) KVR_APP(4, 2) KVR_APP(4, 4) KVR_APP(4, 8) KVR_APP(8, 2) KVR_APP(8, 4) KVR_APP(8, 8)
 #undef KVR_APP
     return check_launch();
   }
-  append_kernel<<<grid_for(total, kTokWarps), kTokWarps * 32, 0, s>>>(*a, lengths, advance);
+  (void)pdl_launch(append_kernel, dim3(grid_for(total, kTokWarps)), dim3(kTokWarps * 32), 0, s, 1, *a, lengths,
+                   advance);
   return check_launch();
 }
 
