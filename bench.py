@@ -625,7 +625,9 @@ def run_draft_loop(args, wl, world, rank, local):
                 "graph_us_per_draft_step": us_step, "eager_us_per_draft_step": eager_ms * 1e3 / steps,
                 "achieved_gbs": step_bytes / (us_step * 1e-6) / 1e9 * world,
                 "frac_of_peak_per_gpu": step_bytes / (us_step * 1e-6) / 1e9 / peak, "peak_source": peak_src,
-                "append_errors": errors, "gpu_launches": args.steps * steps * wl.layers * 3}
+                "append_errors": errors,
+                # one launch per layer and draft step: the decode appends the token itself
+                "gpu_launches": args.steps * steps * wl.layers}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -249,6 +249,20 @@ int kvr_decode_attention_lengths(const kvr_decode_args* a, const int* lengths, i
 size_t kvr_decode_simt_workspace(const kvr_decode_args* a);
 int kvr_decode_attention_simt(const kvr_decode_args* a, kvr_stream_t stream);
 
+/* One decode step with the append fused in: the new token's key row
+ * (k_new, [B, HKV, 1, D] bf16) goes to the BF16 residual and its value row
+ * (v_new) is quantized per token, exactly as kvr_append_lengths with n = 1,
+ * by the decode launch itself -- the CTA whose split holds the new token
+ * stores it before reading its first chunk -- and the decode then attends
+ * over the sequence including it; lengths advance by one (their last CTA to
+ * read them moves them).  a and residual_capacity as for
+ * kvr_decode_attention_lengths, with n_layers == 1; a step past a capacity
+ * sets lengths[2] and decodes without appending.  Replaces the two launches
+ * of kvr_append_lengths + kvr_decode_attention_lengths (PackedLayer.append
+ * then the attention call, packed_review.py:23-31 and :78).              */
+int kvr_decode_step(const kvr_decode_args* a, const uint16_t* k_new, const uint16_t* v_new, int* lengths,
+                    int residual_capacity, kvr_stream_t stream);
+
 /* LSE merge of externally produced partials (the cross-GPU token split):
  * parts: n_parts blocks of [rows] (m, l) pairs and [rows, D] unnormalised
  * outputs, m in log2 units; out[rows, D] bf16 = sum_p 2^(m_p-M) o_p /

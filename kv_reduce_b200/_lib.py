@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "kvr_advance_lengths",
     "kvr_set_lengths",
     "kvr_decode_attention_lengths",
+    "kvr_decode_step",
     "kvr_exchange_merge",
     "kvr_exchange_alloc",
     "kvr_exchange_open",
@@ -186,6 +187,7 @@ def load() -> ctypes.CDLL:
     lib.kvr_advance_lengths.argtypes = [c_void_p, c_int, c_void_p]
     lib.kvr_set_lengths.argtypes = [c_void_p, c_int, c_int, c_void_p]
     lib.kvr_decode_attention_lengths.argtypes = [POINTER(DecodeArgs), c_void_p, c_int, c_void_p]
+    lib.kvr_decode_step.argtypes = [POINTER(DecodeArgs), c_void_p, c_void_p, c_void_p, c_int, c_void_p]
     lib.kvr_exchange_merge.argtypes = [POINTER(ExchangeArgs), c_void_p]
     lib.kvr_exchange_alloc.argtypes = [c_size_t, POINTER(c_void_p), ctypes.c_char_p]
     lib.kvr_exchange_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]

@@ -109,6 +109,52 @@ __device__ __forceinline__ float affine_dequant(uint32_t code, float scale, floa
   return __fadd_rn(__fmul_rn(static_cast<float>(code), scale), offset);
 }
 
+// Exact affine code with a reciprocal.  q = fl(x - mn) * fl(1/scale) is
+// within 1.5 * 2^-23 * q of the reference's quotient fl(fl(x - mn) / scale)
+// (< 5e-5 for codes up to 255), so both round to the same integer unless q
+// lies within that distance of n + 0.5; within 1e-3 of it the exact IEEE
+// division decides.
+static __device__ __noinline__ float exact_quotient(float diff, float scale) { return __fdiv_rn(diff, scale); }
+
+static __device__ __forceinline__ uint32_t affine_code_rcp(float x, float mn, float scale, float inv, int levels) {
+  const float diff = __fsub_rn(x, mn);
+  float q = __fmul_rn(diff, inv);
+  float r = rintf(q);
+  if (fabsf(q - r) > 0.5f - 1e-3f) r = rintf(exact_quotient(diff, scale));   // near n + 0.5: rare
+  r = fminf(fmaxf(r, 0.f), (float)levels);
+  return (uint32_t)r;
+}
+
+// N bf16 values (N in {2, 4, 8}) as fp32, from one vector load.
+template <int N>
+static __device__ __forceinline__ void load_bf16x(const uint16_t* p, float (&v)[N]) {
+  uint32_t w[N / 2];
+  if constexpr (N == 2) {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else if constexpr (N == 4) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    w[0] = x.x; w[1] = x.y;
+  } else {
+    const uint4 x = *reinterpret_cast<const uint4*>(p);
+    w[0] = x.x; w[1] = x.y; w[2] = x.z; w[3] = x.w;
+  }
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    v[2 * i] = bf16lo(w[i]);
+    v[2 * i + 1] = bf16hi(w[i]);
+  }
+}
+
+// Store the low NB bytes of `w` (NB in {1, 2, 4, 8}).
+template <int NB>
+static __device__ __forceinline__ void store_bytes(uint8_t* p, uint64_t w) {
+  if constexpr (NB == 1) *p = (uint8_t)w;
+  else if constexpr (NB == 2) *reinterpret_cast<uint16_t*>(p) = (uint16_t)w;
+  else if constexpr (NB == 4) *reinterpret_cast<uint32_t*>(p) = (uint32_t)w;
+  else *reinterpret_cast<uint2*>(p) = make_uint2((uint32_t)w, (uint32_t)(w >> 32));
+}
+
+
 // Byte `byte_idx` of the LSB-first bitstream of `codes` (bits per code),
 // reading codes from `get(i)` for i in [0, n).  Works for any bits in 1..8.
 template <typename Get>

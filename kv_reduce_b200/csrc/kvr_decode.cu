@@ -122,10 +122,54 @@ struct Params {
   int* cnt2;                     // [units]
   float* out_ml;                 // partial mode: (m, l) per (layer, b, hq)
   float* out_o;                  // partial mode: unnormalised o
-  const int* dev_len;            // non-null: sequence / prefix length read here at run time
+  int* dev_len;                  // non-null: sequence / prefix length read here at run time
   int res_cap;                   // residual rows the key residual buffer holds
   int cluster;                   // > 1: launched in clusters of NS CTAs, one per unit
+  // fused append of one new token per (b, kv head) before the decode
+  // (device-side lengths only): its key row goes to the BF16 residual, its
+  // value row is quantized per token, and the sequence length advances
+  const uint16_t* app_k;         // [B, HKV, 1, D] bf16, or null
+  const uint16_t* app_v;
 };
+
+// Append one token of unit bh (one warp; lane = D/32 channels): the key row
+// into the BF16 residual at res_row, the value row quantized per token into
+// row s of the value payload and metadata -- the arithmetic of the append
+// kernel (exact min/max, IEEE scale, affine_code_rcp), so the bytes match it.
+template <int D, int VB, typename P>
+__device__ __forceinline__ void append_token(const P& p, const LayerPtrs& Lp, int bh, int s, int res_row, int lane) {
+  constexpr int K = D / 32;
+  constexpr int LB = K * VB / 8;
+  constexpr int levels = (1 << VB) - 1;
+  const int64_t src = (int64_t)bh * D + lane * K;
+  uint16_t* kr = const_cast<uint16_t*>(Lp.kr) + (int64_t)bh * p.kr_bh + (int64_t)res_row * D + lane * K;
+  if constexpr (K == 2) *reinterpret_cast<uint32_t*>(kr) = *reinterpret_cast<const uint32_t*>(p.app_k + src);
+  else *reinterpret_cast<uint2*>(kr) = *reinterpret_cast<const uint2*>(p.app_k + src);
+  float xv[K];
+  load_bf16x<K>(p.app_v + src, xv);
+  float mn = xv[0], mx = xv[0];
+#pragma unroll
+  for (int k = 1; k < K; ++k) {
+    mn = fminf(mn, xv[k]);
+    mx = fmaxf(mx, xv[k]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const float scale = affine_scale(mn, mx, VB);
+  const float inv = __frcp_rn(scale);
+  uint64_t w = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k) w |= (uint64_t)affine_code_rcp(xv[k], mn, scale, inv, levels) << (k * VB);
+  store_bytes<LB>(const_cast<uint8_t*>(Lp.vp) + (int64_t)bh * p.vp_bh + (int64_t)s * (32 * LB) + lane * LB, w);
+  if (lane == 0) {
+    const int64_t m = (int64_t)bh * p.vm_bh + s;
+    const_cast<uint16_t*>(Lp.vs)[m] = f32_to_bf16_bits(scale);
+    const_cast<uint16_t*>(Lp.vo)[m] = f32_to_bf16_bits(mn);
+  }
+}
 
 // ------------------------------------------------------- thread-block clusters
 __device__ __forceinline__ void cluster_sync_all() {
@@ -370,11 +414,32 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
   // clamped to the capacities the host validated: sequence <= tok_end,
   // prefix <= P in whole groups, residual rows <= res_cap.
   int P = p.P, t_end = p.tok_end;
+  int s_new = -1, res_new = 0;   // fused append: the new token's row and residual row
   if (p.dev_len) {
     const int dl_s = *reinterpret_cast<const volatile int*>(p.dev_len);
     const int dl_p = *reinterpret_cast<const volatile int*>(p.dev_len + 1);
+    int S = dl_s;
+    if (p.app_k) {
+      // room for the token, as the append kernel checks it; a step past a
+      // capacity sets the error flag and decodes without appending
+      const bool ok = dl_p >= 0 && dl_p <= dl_s && dl_s + 1 <= p.tok_end && dl_s - dl_p + 1 <= p.res_cap;
+      if (ok) {
+        s_new = dl_s;
+        res_new = dl_s - dl_p;
+        S = dl_s + 1;
+      }
+      if (threadIdx.x == 0) {
+        if (!ok && blockIdx.x == 0) atomicOr(p.dev_len + 2, 1);
+        // every CTA has read the lengths before the last one advances them
+        __threadfence();
+        if (atomicAdd(p.dev_len + 3, 1) == (int)gridDim.x - 1) {
+          p.dev_len[3] = 0;
+          if (ok) p.dev_len[0] = S;
+        }
+      }
+    }
     P = min(max(dl_p, 0), p.P) >> log2G << log2G;
-    t_end = min(min(max(dl_s, P), p.tok_end), P + p.res_cap);
+    t_end = min(min(max(S, P), p.tok_end), P + p.res_cap);
   }
   uint8_t* ring = smem + warp * C::RING;
   const uint32_t ring_s = smem_u32(ring);
@@ -400,6 +465,12 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     const uint16_t* qrow = Lp.q + ((int64_t)b * p.HQ + kvh * p.gqa + (head_ok ? g : 0)) * D;
 
     __syncthreads();   // previous item's merge area (aliases the rings) is dead
+    if (s_new >= 0 && sp == (s_new / kChunk - p.tok_begin / kChunk) / p.chunks_per_split) {
+      // this split holds the new token: store it before any chunk is read
+      if (warp == 0) append_token<D, VB>(p, Lp, bh, s_new, res_new, lane);
+      __threadfence();
+      __syncthreads();
+    }
 
     // ---------------------------------------------------------- chunk range
     const int c_first = p.tok_begin / kChunk;
@@ -1124,6 +1195,8 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   p.dev_len = nullptr;
   p.res_cap = a->seq_len - a->prefix_len;
   p.cluster = pl.cluster;
+  p.app_k = nullptr;
+  p.app_v = nullptr;
 }
 
 // Per-device, per-instantiation set-up: dynamic shared memory limit and
@@ -1211,7 +1284,8 @@ static void launch(const Params<MAXL>& p, const Plan& pl, cudaStream_t s) {
 
 template <int D, int KB, int VB>
 static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float* out_o, cudaStream_t s,
-                 Plan* plan_only, const int* dev_len, int res_cap) {
+                 Plan* plan_only, const int* dev_len, int res_cap, const uint16_t* app_k,
+                 const uint16_t* app_v) {
   using C = Cfg<D, KB, VB>;
   int occ = 3;
   const int dev_st = (a->n_layers == 1) ? prepare<D, KB, VB, 1>(&occ) : prepare<D, KB, VB, KVR_MAX_LAYERS>(&occ);
@@ -1232,27 +1306,30 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
     Params<1> p;
     fill_params(p, a, pl, tb, te);
     p.out_ml = out_ml; p.out_o = out_o;
-    if (dev_len) { p.dev_len = dev_len; p.res_cap = res_cap; }
+    if (dev_len) { p.dev_len = const_cast<int*>(dev_len); p.res_cap = res_cap; }
+    p.app_k = app_k; p.app_v = app_v;
     launch<D, KB, VB, 1>(p, pl, s);
   } else {
     pl.cluster = cluster_for<D, KB, VB, KVR_MAX_LAYERS>(pl);
     Params<KVR_MAX_LAYERS> p;
     fill_params(p, a, pl, tb, te);
     p.out_ml = out_ml; p.out_o = out_o;
-    if (dev_len) { p.dev_len = dev_len; p.res_cap = res_cap; }
+    if (dev_len) { p.dev_len = const_cast<int*>(dev_len); p.res_cap = res_cap; }
+    p.app_k = app_k; p.app_v = app_v;
     launch<D, KB, VB, KVR_MAX_LAYERS>(p, pl, s);
   }
   return check_launch();
 }
 
 static int run(const kvr_decode_args* a, int tb, int te, float* out_ml, float* out_o, cudaStream_t s,
-               Plan* plan_only = nullptr, const int* dev_len = nullptr, int res_cap = 0) {
+               Plan* plan_only = nullptr, const int* dev_len = nullptr, int res_cap = 0,
+               const uint16_t* app_k = nullptr, const uint16_t* app_v = nullptr) {
   int st = validate(a);
   if (st != KVR_OK) return st;
   if (tb < 0 || te > a->seq_len || tb >= te || tb % kChunk) return KVR_ERR_INVALID_ARGUMENT;
 #define KVR_CASE(D_, KB_, VB_)                                                              \
   if (a->head_dim == D_ && a->key_bits == KB_ && a->value_bits == VB_)                      \
-    return run_t<D_, KB_, VB_>(a, tb, te, out_ml, out_o, s, plan_only, dev_len, res_cap);
+    return run_t<D_, KB_, VB_>(a, tb, te, out_ml, out_o, s, plan_only, dev_len, res_cap, app_k, app_v);
   KVR_CASE(128, 4, 4) KVR_CASE(128, 8, 4) KVR_CASE(128, 4, 8) KVR_CASE(128, 8, 8)
   KVR_CASE(128, 2, 2) KVR_CASE(128, 2, 4) KVR_CASE(128, 4, 2) KVR_CASE(128, 8, 2) KVR_CASE(128, 2, 8)
   KVR_CASE(64, 4, 4) KVR_CASE(64, 8, 4) KVR_CASE(64, 4, 8) KVR_CASE(64, 8, 8) KVR_CASE(64, 2, 4)
@@ -1288,6 +1365,16 @@ extern "C" int kvr_decode_attention_lengths(const kvr_decode_args* a, const int*
   if (!a || !lengths || residual_capacity < 0) return KVR_ERR_INVALID_ARGUMENT;
   if (a->seq_len - a->prefix_len > residual_capacity) return KVR_ERR_INVALID_ARGUMENT;
   return dec::run(a, 0, a->seq_len, nullptr, nullptr, as_stream(stream), nullptr, lengths, residual_capacity);
+}
+
+extern "C" int kvr_decode_step(const kvr_decode_args* a, const uint16_t* k_new, const uint16_t* v_new, int* lengths,
+                               int residual_capacity, kvr_stream_t stream) {
+  if (!a || !lengths || !k_new || !v_new || residual_capacity < 0 || a->n_layers != 1)
+    return KVR_ERR_INVALID_ARGUMENT;
+  if (a->seq_len - a->prefix_len > residual_capacity) return KVR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(k_new) || !aligned16(v_new)) return KVR_ERR_MISALIGNED;
+  return dec::run(a, 0, a->seq_len, nullptr, nullptr, as_stream(stream), nullptr, lengths, residual_capacity, k_new,
+                  v_new);
 }
 
 extern "C" int kvr_decode_partial(const kvr_decode_args* a, int token_begin, int token_end, float* part_ml,

@@ -95,10 +95,8 @@ class DraftLoop:
     @staticmethod
     def _issue(work: List, stream: int) -> None:
         lib = _lib.load()
-        for a, dl, launch, res_cap in work:
-            _lib.check("kvr_append_lengths", lib.kvr_append_lengths(a, dl, 1, stream))
-            _lib.check("kvr_decode_attention_lengths",
-                       lib.kvr_decode_attention_lengths(launch.args, dl, res_cap, stream))
+        for a, dl, launch, res_cap in work:   # one token per step: the decode launch appends it
+            _lib.check("kvr_decode_step", lib.kvr_decode_step(launch.args, a.k, a.v, dl, res_cap, stream))
 
     def capture(self) -> None:
         """Record the loop into a CUDA graph (the lengths do not move)."""

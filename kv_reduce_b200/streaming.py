@@ -244,10 +244,12 @@ class PackedKVCacheLayer:
 
     def decode_step(self, query: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, split_tokens: int = 0,
                     out: torch.Tensor | None = None) -> torch.Tensor:
-        """append(k, v) then attention(query) as two library calls.
+        """append(k, v) then attention(query): for one new token a single
+        decode launch that stores the token before attending
+        (kvr_decode_step), else an append and a decode call.
 
-        Both read the lengths from the layer's device-side copy and the
-        append moves it on itself, so the host only rewrites the query,
+        Both forms read the lengths from the layer's device-side copy and
+        move it on themselves, so the host only rewrites the query,
         new-token and output pointers of argument blocks prepared once per
         buffer layout (and the calls can be captured in a CUDA graph).  The
         decode is planned for the buffers' capacity.  The residual buffer is
@@ -282,9 +284,13 @@ class PackedKVCacheLayer:
         launch.layers[0].query, launch.layers[0].out = query.data_ptr(), out.data_ptr()
         dl = self.device_lengths().data_ptr()
         lib = _lib.load()
-        _lib.check("kvr_append_lengths", lib.kvr_append_lengths(app, dl, 1, stream))
-        _lib.check("kvr_decode_attention_lengths",
-                   lib.kvr_decode_attention_lengths(launch.args, dl, self.cap_residual, stream))
+        if n == 1:   # the decode launch appends the token itself
+            _lib.check("kvr_decode_step", lib.kvr_decode_step(launch.args, k.data_ptr(), v.data_ptr(), dl,
+                                                              self.cap_residual, stream))
+        else:
+            _lib.check("kvr_append_lengths", lib.kvr_append_lengths(app, dl, 1, stream))
+            _lib.check("kvr_decode_attention_lengths",
+                       lib.kvr_decode_attention_lengths(launch.args, dl, self.cap_residual, stream))
         self.seq_len += n
         return out
 
