@@ -94,8 +94,9 @@ def test_capacity_is_checked_before_replay(kvr):
 
 
 def test_decode_step_matches_append_then_attention(kvr):
-    """PackedKVCacheLayer.decode_step (two library calls from device-side
-    lengths) == append + packed_kv_decode_attention: same cache bytes,
+    """PackedKVCacheLayer.decode_step (one token: one decode launch that
+    appends it, lengths in device memory) == append +
+    packed_kv_decode_attention: same cache bytes,
     outputs within bf16 rounding; across a commit and a capacity growth."""
     a_cache, b_cache = make_cache(kvr, seed=3, capacity=768), make_cache(kvr, seed=3, capacity=768)
     g = torch.Generator(device="cuda").manual_seed(21)
@@ -113,3 +114,36 @@ def test_decode_step_matches_append_then_attention(kvr):
     same_cache(a_cache, b_cache)
     with pytest.raises(ValueError):
         a_cache.layers[0].decode_step(q[:, :, :, :64], k, v)
+
+
+def test_decode_step_two_tokens_and_capacity_flag(kvr):
+    """decode_step with two new tokens (an append launch and a decode launch)
+    == append + attention, cache bytes equal; and kvr_decode_step with the
+    sequence already at capacity sets the error flag, leaves the lengths
+    where they were and appends nothing."""
+    from kv_reduce_b200 import _lib
+
+    a_cache, b_cache = make_cache(kvr, seed=5), make_cache(kvr, seed=5)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    la, lb = a_cache.layers[0], b_cache.layers[0]
+    q = torch.randn(B, HQ, 1, D, generator=g, device="cuda").to(torch.bfloat16)
+    k2 = torch.randn(B, H, 2, D, generator=g, device="cuda").to(torch.bfloat16)
+    v2 = torch.randn(B, H, 2, D, generator=g, device="cuda").to(torch.bfloat16)
+    got = la.decode_step(q, k2, v2)
+    lb.append(k2, v2)
+    close(got, kvr.packed_kv_decode_attention(q, lb.k, lb.v))
+    same_cache(a_cache, b_cache)
+
+    layer = a_cache.layers[1]
+    k1, v1 = k2[:, :, :1].contiguous(), v2[:, :, :1].contiguous()
+    out = torch.empty_like(q)
+    stream = _lib.stream_ptr(q.device)
+    _, launch = layer._prepare_step(HQ, 0, stream, q, out)
+    dl = layer.device_lengths()
+    dl[0] = layer.capacity                  # no room for one more token
+    payload_before = layer.value_payload.clone()
+    _lib.check("kvr_decode_step", _lib.load().kvr_decode_step(launch.args, k1.data_ptr(), v1.data_ptr(),
+                                                              dl.data_ptr(), layer.cap_residual, stream))
+    torch.cuda.synchronize()
+    assert int(dl[2]) == 1 and int(dl[0]) == layer.capacity and int(dl[3]) == 0
+    assert torch.equal(layer.value_payload, payload_before)
