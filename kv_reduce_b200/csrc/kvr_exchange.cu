@@ -27,6 +27,7 @@ namespace kvr {
 namespace xchg {
 
 constexpr int kThreads = 256;
+constexpr int kPushCtas = 16;   // CTAs that store to the peers (and fence)
 
 __device__ __forceinline__ void store_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
@@ -50,24 +51,33 @@ __global__ void __launch_bounds__(kThreads) exchange_merge_kernel(kvr_exchange_a
   const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
 
-  // 1. push this rank's slot to every peer (the local copy is already in place)
-  const float* mine = a.recv[rank] + ((int64_t)par * world + rank) * slot;
-  for (int p = 0; p < world; ++p) {
-    if (p == rank) continue;
-    float* dst = a.recv[p] + ((int64_t)par * world + rank) * slot;
-    if ((slot & 3) == 0) {
-      const float4* s4 = reinterpret_cast<const float4*>(mine);
-      float4* d4 = reinterpret_cast<float4*>(dst);
-      for (int64_t i = gtid; i < slot / 4; i += gstride) d4[i] = s4[i];
-    } else {
-      for (int64_t i = gtid; i < slot; i += gstride) dst[i] = mine[i];
+  // 1. push this rank's slot to every peer (the local copy is already in
+  //    place).  Only the first kPushCtas CTAs store: a slot is a few hundred
+  //    KB, and each storing CTA must wait for its remote stores to land
+  //    (a system-scope fence) before it arrives -- with every CTA storing a
+  //    sliver, those fences dominated the exchange.
+  const int npush = min((int)gridDim.x, kPushCtas);
+  if ((int)blockIdx.x < npush) {
+    const float* mine = a.recv[rank] + ((int64_t)par * world + rank) * slot;
+    const int64_t ptid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t pstride = (int64_t)npush * blockDim.x;
+    for (int p = 0; p < world; ++p) {
+      if (p == rank) continue;
+      float* dst = a.recv[p] + ((int64_t)par * world + rank) * slot;
+      if ((slot & 3) == 0) {
+        const float4* s4 = reinterpret_cast<const float4*>(mine);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (int64_t i = ptid; i < slot / 4; i += pstride) d4[i] = s4[i];
+      } else {
+        for (int64_t i = ptid; i < slot; i += pstride) dst[i] = mine[i];
+      }
     }
   }
 
   // 2. grid-wide arrival; the last CTA signals every peer
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    if ((int)blockIdx.x < npush) __threadfence_system();   // this CTA's peer stores have landed
     if (atomicAdd(a.counter, 1) == (int)gridDim.x - 1) {
       __threadfence_system();   // every CTA's peer stores precede the signals
       *a.counter = 0;
