@@ -444,8 +444,9 @@ def run_split_sequence(args, wl, world, rank, local):
 
     Each rank packs every layer and keeps its 32-token-aligned token shard
     (kv_reduce_b200.distributed.shard_component); a step is one partial
-    decode launch over all layers of the shard, an NCCL all-gather of the
-    (m, l, o) partials and the LSE merge kernel.  The step time is the max
+    decode launch over all layers of the shard and one exchange kernel that
+    stores the (m, l, o) partials into every peer over NVLink and merges
+    them (--nccl-exchange: an NCCL all-gather and the LSE merge kernel).  The step time is the max
     over ranks; `value` counts the whole sequence's bytes once.
     """
     import torch.distributed as dist
