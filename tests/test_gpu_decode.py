@@ -295,23 +295,25 @@ def test_packed_decoder_equals_per_layer_calls(kvr):
         dec(q_all.float())
 
 
-def test_packed_decoder_host_step(kvr):
+@pytest.mark.parametrize("layers,out_dtype", [(3, torch.bfloat16), (35, torch.float32)])
+def test_packed_decoder_host_step(kvr, layers, out_dtype):
     """PackedDecoder.host_step (pinned host queries in, pinned host outputs
     out; the first call eager, later calls a replayed CUDA graph of copy-in,
     decode and copy-out) == the device-buffer call, bit for bit, across
-    steps with new query values written into the same host buffer."""
+    steps with new query values written into the same host buffer; 35
+    layers take two launches per step."""
     from kv_reduce_b200 import workloads
 
-    wl = workloads.CONFIGS["2"].scaled(seq_len=2100, layers=3)
+    wl = workloads.CONFIGS["2"].scaled(seq_len=2100, layers=layers)
     ks, vs = [], []
     for layer in range(wl.layers):
         k, v = workloads.make_layer_kv(wl, layer)
         pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
         ks.append(pk)
         vs.append(pv)
-    dec = kvr.PackedDecoder(ks, vs, q_heads=wl.q_heads)
+    dec = kvr.PackedDecoder(ks, vs, q_heads=wl.q_heads, out_dtype=out_dtype)
     q_host = torch.empty(dec.q_shape, dtype=torch.bfloat16).pin_memory()
-    o_host = torch.empty(dec.q_shape, dtype=torch.bfloat16).pin_memory()
+    o_host = torch.empty(dec.q_shape, dtype=out_dtype).pin_memory()
     for step in range(3):
         q = torch.stack([workloads.make_query(wl, layer, step=step) for layer in range(wl.layers)])
         q_host.copy_(q.cpu())
