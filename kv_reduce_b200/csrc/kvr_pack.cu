@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(kTokWarps * 32) append_kernel(kvr_append_args 
 
 // Append, vectorised (D in {64,128,256}, 2/4/8-bit values): a warp per new
 // token row; lane l copies key channels [l*K, l*K+K) and quantizes the same
-// value channels in registers (as quant_token_fast).
+// value channels in registers (min/max by warp shuffles, the per-token rule).
 template <int K, int BITS>
 __global__ void __launch_bounds__(256) append_fast(kvr_append_args a, int* lengths, int advance) {
   pdl_enter();
