@@ -14,10 +14,26 @@ K4V4, key group 32, 128-token BF16 residual window, batch 1).
   e2e    : the same metric through the public Python API with the queries
            copied host->device and the outputs device->host every step.
 
-With --gpus N (torchrun) each rank holds its own batch-1 sequence (weak
-scaling, batch sharding, no collective on the data path); the step time is
-the max over ranks.  ``--impl reference`` times the reference's unfused CPU
-path (unpack + SDPA, restated in oracle/cpu_baseline.py) on the host cores.
+  workloads : the other benchmark workloads on the same kernel, each with
+           its own clock record: Llama-3.2-1B geometry batch 32 x 8K K8V4 and
+           K4V8, Qwen geometry batch 64 x 16K K2V2 (one launch per step), and
+           the speculative draft loop (batch 128 x 4K, four steps of append +
+           decode per round, replayed as a CUDA graph).  At N > 1 their global
+           batch is sharded across the ranks.
+
+With --gpus N (torchrun) each rank holds its own batch-1 sequence for the
+headline (weak scaling, batch sharding, no collective on the data path); the
+step time is the max over ranks.  At N > 1 the line also carries
+`split_sequence`: ONE batch-1 32K sequence with its tokens split across the
+ranks (partial decode + the fused NVLink exchange and LSE merge kernel).
+``--impl reference`` times the reference's unfused CPU path (unpack + SDPA,
+restated in oracle/cpu_baseline.py) on the host cores.
+
+Tools on the same workloads (not part of the driver's line):
+  --engine-ab     tensor cores vs CUDA cores for the decode (one JSON line per
+                  workload and engine)
+  --all-kernels   every library kernel once per round, for a profiler's
+                  launch list
 """
 from __future__ import annotations
 
@@ -59,6 +75,12 @@ def parse_args():
     p.add_argument("--split-sequence", action="store_true",
                    help="N>1: split ONE batch-1 sequence's tokens across the ranks (strong scaling, "
                         "partial decode + NCCL all-gather + LSE merge) instead of one sequence per rank")
+    p.add_argument("--no-workloads", action="store_true", help="headline workload only")
+    p.add_argument("--workload-steps", type=int, default=10, help="timed steps per extra workload")
+    p.add_argument("--engine-ab", action="store_true", help="tool: tensor cores vs CUDA cores (see --configs)")
+    p.add_argument("--configs", default="2,4", help="--engine-ab workloads")
+    p.add_argument("--all-kernels", action="store_true", help="tool: run every library kernel (see --repeat)")
+    p.add_argument("--repeat", type=int, default=2, help="--all-kernels rounds after one warm-up round")
     return p.parse_args()
 
 
@@ -183,6 +205,20 @@ def cpu_baseline_sample(wl, seconds: float, layer_bytes: int):
             "ms_per_layer": dt * 1e3, "ms_per_step_extrapolated": dt * 1e3 * wl.layers}
 
 
+def workload_config(wl, world, args, batch_sharded_global=False):
+    """The `config` object of a line, the same for our arm and the reference arm."""
+    from kv_reduce_b200 import workloads
+
+    step_bytes = workloads.layer_bytes(wl)["total"] * wl.layers
+    per_gpu = wl.batch if not batch_sharded_global else -(-wl.batch // world)
+    glob = wl.batch * world if not batch_sharded_global else wl.batch
+    return {"workload": wl.name, "layers": wl.layers, "batch_per_gpu": per_gpu, "global_batch": glob,
+            "seq_len": wl.seq_len, "q_heads": wl.q_heads, "kv_heads": wl.kv_heads, "head_dim": wl.head_dim,
+            "kv_bits": f"K{wl.k_bits}V{wl.v_bits}", "group_size": wl.group_size, "residual": wl.residual_length,
+            "parallelism": f"batch-sharded x{world}", "split_tokens": args.split_tokens,
+            "l2": f"inputs {step_bytes / 1e6:.0f} MB per step > 126 MB L2; layers rotate, no flush"}
+
+
 def run_reference(args, wl, world, rank):
     from kv_reduce_b200 import workloads
 
@@ -207,16 +243,15 @@ def run_reference(args, wl, world, rank):
         times.append(time.perf_counter() - t0)
     dt = sum(times) / len(times)
     value = lb / dt / 1e9
-    sample = f"one {wl.seq_len}-token layer per step (of {wl.layers}), unpack + SDPA in bf16 on host cores"
+    sample = (f"one {wl.seq_len}-token layer per step (of {wl.layers}), unpack + SDPA in bf16 on host cores, "
+              f"the reference's unfused path restated by the oracle port")
     line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dt * 1e3 * wl.layers, "ms_per_step_note": "extrapolated: layer time x layers",
+            "warmup": args.warmup, "ms_per_step": dt * 1e3 * wl.layers,
+            "ms_per_step_note": "extrapolated: layer time x layers",
             "us_per_step": dt * 1e6 * wl.layers,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": wl.name, "layers": wl.layers, "batch": wl.batch, "seq_len": wl.seq_len,
-                       "q_heads": wl.q_heads, "kv_heads": wl.kv_heads, "head_dim": wl.head_dim,
-                       "kv_bits": f"K{wl.k_bits}V{wl.v_bits}", "group_size": wl.group_size,
-                       "residual": wl.residual_length},
+            "config": workload_config(wl, world, args),
             "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -224,20 +259,27 @@ def run_reference(args, wl, world, rank):
 
 
 # ------------------------------------------------------------------ our arm
-def build_cache(wl, device, rank):
+def build_cache(wl, device, rank, batch_range=None):
+    """Packed caches, queries of every layer.  batch_range=(a, b) keeps the
+    sequences [a, b) of the workload's batch (the data of a sequence does not
+    depend on how the batch is sharded)."""
     import kv_reduce_b200 as kvr
     from kv_reduce_b200 import workloads
 
-    seed_wl = wl.scaled(seed=wl.seed + 100 * rank)
+    seed_wl = wl.scaled(seed=wl.seed + 100 * rank) if batch_range is None else wl
     ks, vs, qs = [], [], []
     for layer in range(wl.layers):
         k, v = workloads.make_layer_kv(seed_wl, layer, device=device)
+        q = workloads.make_query(seed_wl, layer, device=device)
+        if batch_range is not None:
+            a, b = batch_range
+            k, v, q = k[a:b].contiguous(), v[a:b].contiguous(), q[a:b].contiguous()
         pk, pv = kvr.pack_kivi_kv(k, v, k_bits=wl.k_bits, v_bits=wl.v_bits, group_size=wl.group_size,
                                   residual_length=wl.residual_length)
         del k, v
         ks.append(pk)
         vs.append(pv)
-        qs.append(workloads.make_query(seed_wl, layer, device=device))
+        qs.append(q)
     torch.cuda.synchronize(device)
     return ks, vs, qs
 
@@ -280,29 +322,271 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
-def run_ours(args, wl, world, rank, local):
+def sum_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def fused_launches(ks, vs, qs, device, stream, split_tokens):
+    """All layers of a step in one launch per <= 32 layers (layer index in the grid)."""
+    from kv_reduce_b200.packed_kv_attention import DecodeLaunch, _geometry, _layer_ptrs
+
+    outs = [torch.empty_like(q) for q in qs]
+    geom = _geometry(qs[0], ks[0], vs[0])
+    ptrs = [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, outs, ks, vs)]
+    launches = [DecodeLaunch(geom, ptrs[i:i + 32], device, split_tokens=split_tokens, stream=stream.cuda_stream)
+                for i in range(0, len(ptrs), 32)]
+    return launches, outs, geom, ptrs
+
+
+def measure_workload(args, key, world, rank, device, pg_sync):
+    """One extra workload on the fused kernel, its global batch sharded over
+    the ranks; returns its sub-dict (rank 0) with its own clock record."""
+    from kv_reduce_b200 import distributed as kd
+    from kv_reduce_b200 import workloads
+
+    wl = workloads.CONFIGS[key]
+    a, b = kd.batch_shard(wl.batch, world, rank)
+    ks, vs, qs = build_cache(wl, device, rank, batch_range=(a, b))
+    stream = torch.cuda.Stream(device)
+    # the outputs must outlive the captured graph: torch.cuda.graph empties the
+    # allocator cache before capture, so a dropped output would be unmapped
+    launches, outs, _, _ = fused_launches(ks, vs, qs, device, stream, args.split_tokens)
+
+    def step():
+        for launch in launches:
+            launch()
+
+    steps = max(1, args.workload_steps)
+    with ClockSampler(device) as clocks:
+        ms = time_graph(step, stream, steps, max(args.warmup, 3), world, pg_sync)
+    ms = max_over_ranks(ms, world, device)
+    step_ms = ms / steps
+    my_bytes = workloads.layer_bytes(wl, batch=b - a)["total"] * wl.layers
+    total_bytes = sum_over_ranks(my_bytes, world, device)
+    peak, _ = measured_peak()
+    gbs = total_bytes / (step_ms * 1e-3) / 1e9
+    res = {"workload": wl.name, "layers": wl.layers, "global_batch": wl.batch, "batch_per_gpu": b - a,
+           "seq_len": wl.seq_len, "kv_bits": f"K{wl.k_bits}V{wl.v_bits}", "head_dim": wl.head_dim,
+           "q_heads": wl.q_heads, "kv_heads": wl.kv_heads,
+           "us_per_step": step_ms * 1e3, "gbps": gbs, "frac": gbs / world / peak, "frac_note": "of measured, per GPU",
+           "bytes_per_step": total_bytes, "num_splits": launches[0].num_splits, "steps": steps,
+           "scaling": "strong (global batch fixed, sharded by batch)" if world > 1 else "n/a",
+           "timing": "all layers per launch, CUDA graph, CUDA events, max over ranks; inputs > L2",
+           "gpu_launches": steps * len(launches), "clocks": clocks.summary()}
+    del launches, outs, ks, vs, qs
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_draft_loop(args, world, rank, device, pg_sync):
+    """The speculative draft loop (batch 128 x 4K, K4V4, 4 steps of append +
+    decode per round) on the streaming cache, the batch sharded over the
+    ranks; µs per draft step of the replayed CUDA graph."""
     import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import distributed as kd
+    from kv_reduce_b200 import workloads
+    from kv_reduce_b200.draft import DraftLoop
+
+    wl = workloads.CONFIGS["5"]
+    a, b = kd.batch_shard(wl.batch, world, rank)
+    steps = max(1, wl.draft_steps or 4)
+    cache = kvr.PackedKVCache(wl.layers, b - a, wl.kv_heads, wl.head_dim, k_bits=wl.k_bits, v_bits=wl.v_bits,
+                              group_size=wl.group_size, residual_length=wl.residual_length,
+                              capacity=wl.seq_len + 64, device=device)
+    for i, layer in enumerate(cache.layers):
+        k, v = workloads.make_layer_kv(wl, i, device=device)
+        layer.prefill(k[a:b].contiguous(), v[a:b].contiguous())
+        del k, v
+    loop = DraftLoop(cache, q_heads=wl.q_heads, steps=steps, split_tokens=args.split_tokens)
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    for t in (loop.q, loop.k, loop.v):
+        t.copy_(torch.randn(t.shape, generator=g, device=device).to(torch.bfloat16))
+    start = cache.get_seq_length()
+    rounds = max(1, args.workload_steps)
+
+    def timed(fn, n):
+        ev = []
+        for i in range(max(args.warmup, 3) + n):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            cache.crop(start)
+            if i >= max(args.warmup, 3):
+                ev.append((e0, e1))
+        torch.cuda.synchronize()
+        return sum(x.elapsed_time(y) for x, y in ev) / len(ev)
+
+    pg_sync()
+    with ClockSampler(device) as clocks:
+        graph_ms = timed(loop.replay, rounds)
+    graph_ms = max_over_ranks(graph_ms, world, device)
+    errors = int(sum_over_ranks(loop.errors(), world, device))
+    wl_b = wl.scaled(batch=b - a)
+    my_bytes = sum(workloads.layer_bytes(wl_b, seq_len=start + t + 1)["total"] for t in range(steps)) / steps
+    my_bytes = my_bytes * wl.layers + wl.layers * (b - a) * wl.kv_heads * (
+        2 * wl.head_dim + wl.head_dim * wl.v_bits // 8 + 4)
+    total_bytes = sum_over_ranks(my_bytes, world, device)
+    us_step = graph_ms * 1e3 / steps
+    peak, _ = measured_peak()
+    gbs = total_bytes / (us_step * 1e-6) / 1e9
+    res = {"workload": wl.name, "layers": wl.layers, "global_batch": wl.batch, "batch_per_gpu": b - a,
+           "seq_len": start, "draft_steps": steps, "kv_bits": f"K{wl.k_bits}V{wl.v_bits}",
+           "us_per_draft_step": us_step, "gbps": gbs, "frac": gbs / world / peak,
+           "frac_note": "of measured, per GPU", "bytes_per_draft_step": total_bytes, "rounds": rounds,
+           "append_errors": errors,
+           "scaling": "strong (global batch fixed, sharded by batch)" if world > 1 else "n/a",
+           "timing": "CUDA graph of one round of draft steps (one append+decode launch per layer and step, "
+                     "device-side lengths), CUDA events per round, rolled back between rounds, max over ranks",
+           "gpu_launches": rounds * steps * wl.layers, "clocks": clocks.summary()}
+    del loop, cache
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_split_sequence(args, wl, world, rank, device, nccl_exchange=False):
+    """One batch-1 sequence, its tokens split across the ranks (strong scaling).
+
+    Each rank packs every layer and keeps its 32-token-aligned token shard
+    (kv_reduce_b200.distributed.shard_component); a step is one partial
+    decode launch over all layers of the shard and one exchange kernel that
+    stores the (m, l, o) partials into every peer over NVLink and merges
+    them (nccl_exchange: an NCCL all-gather and the LSE merge kernel).  The
+    step time is the max over ranks; the result counts the whole sequence's
+    bytes once.  Returns the sub-dict (rank 0) and the exchange error count.
+    """
+    import torch.distributed as dist
+
+    import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import distributed as kd
     from kv_reduce_b200 import workloads
     from kv_reduce_b200.packed_kv_attention import DecodeLaunch, _geometry, _layer_ptrs
 
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
+    a, b = kd.token_shards(wl.seq_len, world, align=wl.group_size)[rank]
+    ks, vs, qs = [], [], []
+    for layer in range(wl.layers):
+        k, v = workloads.make_layer_kv(wl, layer, device=device)
+        pk, pv = kvr.pack_kivi_kv(k, v, k_bits=wl.k_bits, v_bits=wl.v_bits, group_size=wl.group_size,
+                                  residual_length=wl.residual_length)
+        sk, sv = kd.shard_component(pk, pv, a, b)
+        del k, v, pk, pv
+        ks.append(sk)
+        vs.append(sv)
+        qs.append(workloads.make_query(wl, layer, device=device))
+    torch.cuda.synchronize()
+    rows = wl.layers * wl.batch * wl.q_heads
+    dummy = [torch.empty_like(q) for q in qs]
+    geom = _geometry(qs[0], ks[0], vs[0])
+    launch = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
+                          split_tokens=args.split_tokens)
+    out = torch.empty(rows, wl.head_dim, dtype=torch.bfloat16, device=device)
+    p2p = world > 1 and not nccl_exchange
+    if p2p:
+        xchg = kd.PeerExchange(rows, wl.head_dim, device)
+
+        def step():
+            xchg.step(launch.partial)
+    else:
+        dec = kd.SequenceShardDecoder(rows, wl.head_dim, world, device, partial_fn=launch.partial,
+                                      merge_fn=lambda ml, o: kvr.lse_merge(ml, o, out=out))
+
+        def step():
+            dec.step()
+
+    for _ in range(2 * ((max(args.warmup, 3) + 1) // 2)):   # an even number: the graph pairs steps
+        step()
+    torch.cuda.synchronize()
+    graph = None
+    if p2p:
+        # both steps of a pair (one per receive half) in one CUDA graph, the
+        # partial launch bound to the capture stream
+        side = torch.cuda.Stream(device)
+        launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
+                                split_tokens=args.split_tokens, stream=side.cuda_stream)
+        graph = xchg.capture_pair(launch_g.partial, side)
+        for _ in range(2):
+            xchg.replay_pair(graph)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    pairs = max(1, args.steps // 2)
+    n_steps = 2 * pairs if graph is not None else args.steps
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        s0.record()
+        if graph is not None:
+            for _ in range(pairs):
+                xchg.replay_pair(graph)
+        else:
+            for _ in range(args.steps):
+                step()
+        s1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(s0.elapsed_time(s1) / n_steps, world, device)
+    errors = xchg.errors() if p2p else 0
+    errors = int(sum_over_ranks(errors, world, device))
+    lb = workloads.layer_bytes(wl)
+    step_bytes = lb["total"] * wl.layers
+    peak, peak_src = measured_peak()
+    value = step_bytes / (ms * 1e-3) / 1e9
+    res = {"workload": wl.name, "layers": wl.layers, "global_batch": wl.batch, "seq_len": wl.seq_len,
+           "parallelism": f"token-split x{world}", "shard_tokens": b - a, "num_splits": launch.num_splits,
+           "us_per_step": ms * 1e3, "gbps": value, "tokens_per_s": wl.batch / (ms * 1e-3),
+           "frac_per_gpu": value / world / peak, "frac_note": "of measured, per GPU", "steps": n_steps,
+           "exchange": ("one kernel: NVLink peer stores + signal + LSE merge" if p2p else
+                        "NCCL all-gather + LSE merge launch" if world > 1 else "none"),
+           "exchange_errors": errors, "scaling": "strong (one sequence)",
+           "timing": ("CUDA graph of two steps (partial decode of all layers + fused exchange)"
+                      if graph is not None else
+                      "eager: partial decode (all layers, one launch) + exchange/merge per step")
+                     + ", CUDA events, max over ranks",
+           "gpu_launches": n_steps * 2, "clocks": clocks.summary()}
+    del graph
+    if p2p:
+        xchg.close()
+    del launch, ks, vs, qs
+    torch.cuda.empty_cache()
+    return res, errors
+
+
+def init_pg(world, device):
     if world > 1:
         import torch.distributed as dist
 
+        # the exchange's peer loads and stores are plain; keep NCCL's own
+        # collectives (barriers, timing reductions) off NVLink multicast too
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-        pg_sync = lambda: (dist.barrier(), torch.cuda.synchronize())  # noqa: E731
-    else:
-        pg_sync = lambda: torch.cuda.synchronize()  # noqa: E731
+        return lambda: (dist.barrier(), torch.cuda.synchronize())
+    return lambda: torch.cuda.synchronize()
+
+
+def close_pg(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_ours(args, wl, world, rank, local):
+    import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import workloads
+    from kv_reduce_b200.packed_kv_attention import DecodeLaunch
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pg_sync = init_pg(world, device)
 
     ks, vs, qs = build_cache(wl, device, rank)
-    outs = [torch.empty_like(q) for q in qs]
-    geom = _geometry(qs[0], ks[0], vs[0])
     stream = torch.cuda.Stream(device)
-    ptrs = [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, outs, ks, vs)]
-    # the whole step in one launch per <= 32 layers (layer index in the grid)
-    fused = [DecodeLaunch(geom, ptrs[i:i + 32], device, split_tokens=args.split_tokens, stream=stream.cuda_stream)
-             for i in range(0, wl.layers, 32)]
+    fused, outs, geom, ptrs = fused_launches(ks, vs, qs, device, stream, args.split_tokens)
     # one launch per layer, as a model calls it
     per_layer = [DecodeLaunch(geom, [p], device, split_tokens=args.split_tokens, stream=stream.cuda_stream)
                  for p in ptrs]
@@ -396,12 +680,33 @@ def run_ours(args, wl, world, rank, local):
         e2e_per_layer = {"value": step_bytes * world / (e2e_pl_ms * 1e-3) / 1e9, "unit": "GB/s",
                          "ms_per_step": e2e_pl_ms,
                          "path": "kv_reduce_b200.packed_kv_decode_attention once per layer (the reference's call)"}
+        del decoder
+
+    num_splits = fused[0].num_splits
+    per_layer_splits = per_layer[0].num_splits
+    n_fused = len(fused)
+    del fused, per_layer, outs, ptrs, ks, vs, qs
+    torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(wl, args.cpu_seconds, lb["total"])
 
+    extra = None
+    if not args.no_workloads:
+        extra = {}
+        for key in ("3a", "3b", "4"):
+            extra[key] = measure_workload(args, key, world, rank, device, pg_sync)
+        extra["5"] = measure_draft_loop(args, world, rank, device, pg_sync)
+
+    split = None
+    split_errors = 0
+    if world > 1 and not args.no_workloads:
+        pg_sync()
+        split, split_errors = measure_split_sequence(args, wl, world, rank, device)
+
     if rank == 0:
+        config = workload_config(wl, world, args)
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "us_per_step": step_ms * 1e3,
@@ -409,14 +714,9 @@ def run_ours(args, wl, world, rank, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "u4 codes; f16/bf16 mma, fp32 accumulate and softmax",
             "data": "synthetic (seeded N(0,1) K/V/Q, outlier key channels)",
-            "config": {"workload": wl.name, "layers": wl.layers, "batch_per_gpu": wl.batch,
-                       "global_batch": wl.batch * world, "seq_len": wl.seq_len, "q_heads": wl.q_heads,
-                       "kv_heads": wl.kv_heads, "head_dim": wl.head_dim, "kv_bits": f"K{wl.k_bits}V{wl.v_bits}",
-                       "group_size": wl.group_size, "residual": wl.residual_length,
-                       "parallelism": f"batch-sharded x{world}", "split_tokens": args.split_tokens,
-                       "num_splits": fused[0].num_splits,
-                       "l2": f"inputs {step_bytes / 1e6:.0f} MB per step > 126 MB L2; layers rotate, no flush",
-                       "timing": "all layers of the step in one launch, CUDA graph, CUDA events, max over ranks"},
+            "config": config,
+            "plan": {"num_splits": num_splits, "per_layer_num_splits": per_layer_splits},
+            "timing": "all layers of the step in one launch, CUDA graph, CUDA events, max over ranks",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(wl.name),
                          "kernel": "kvr::dec::decode_kernel, all layers of the step per launch",
@@ -424,221 +724,164 @@ def run_ours(args, wl, world, rank, local):
                          "frac_note": "of measured" if "measured" in peak_src else "of fallback"},
             "per_layer": {"ms_per_step": layer_step_ms, "us_per_layer": layer_step_ms * 1e3 / wl.layers,
                           "gbps": step_bytes * world / (layer_step_ms * 1e-3) / 1e9,
-                          "num_splits": per_layer[0].num_splits,
+                          "num_splits": per_layer_splits,
                           "timing": "one launch per layer, 28 launches replayed as a CUDA graph"},
             "e2e": e2e, "e2e_layers_call": e2e_layers_call, "e2e_per_layer_calls": e2e_per_layer,
             "cpu_baseline": cpu,
-            "gpu_launches": args.steps * len(fused),
+            "workloads": extra,
+            "split_sequence": split,
+            "gpu_launches": args.steps * n_fused,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-        dist.destroy_process_group()
+    close_pg(world)
+    if split_errors:
+        raise SystemExit(f"{split_errors} exchange wait(s) timed out in the sequence split")
 
 
 def run_split_sequence(args, wl, world, rank, local):
-    """One batch-1 sequence, its tokens split across the ranks (strong scaling).
-
-    Each rank packs every layer and keeps its 32-token-aligned token shard
-    (kv_reduce_b200.distributed.shard_component); a step is one partial
-    decode launch over all layers of the shard and one exchange kernel that
-    stores the (m, l, o) partials into every peer over NVLink and merges
-    them (--nccl-exchange: an NCCL all-gather and the LSE merge kernel).  The step time is the max
-    over ranks; `value` counts the whole sequence's bytes once.
-    """
-    import torch.distributed as dist
-
-    import kv_reduce_b200 as kvr
-    from kv_reduce_b200 import distributed as kd
-    from kv_reduce_b200 import workloads
-    from kv_reduce_b200.packed_kv_attention import DecodeLaunch, _geometry, _layer_ptrs
-
+    """--split-sequence: the sequence split as the whole line."""
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-    a, b = kd.token_shards(wl.seq_len, world, align=wl.group_size)[rank]
-    ks, vs, qs = [], [], []
-    for layer in range(wl.layers):
-        k, v = workloads.make_layer_kv(wl, layer, device=device)
-        pk, pv = kvr.pack_kivi_kv(k, v, k_bits=wl.k_bits, v_bits=wl.v_bits, group_size=wl.group_size,
-                                  residual_length=wl.residual_length)
-        sk, sv = kd.shard_component(pk, pv, a, b)
-        del k, v, pk, pv
-        ks.append(sk)
-        vs.append(sv)
-        qs.append(workloads.make_query(wl, layer, device=device))
-    torch.cuda.synchronize()
-    rows = wl.layers * wl.batch * wl.q_heads
-    dummy = [torch.empty_like(q) for q in qs]
-    geom = _geometry(qs[0], ks[0], vs[0])
-    launch = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
-                          split_tokens=args.split_tokens)
-    out = torch.empty(rows, wl.head_dim, dtype=torch.bfloat16, device=device)
-    p2p = world > 1 and not args.nccl_exchange
-    if p2p:
-        xchg = kd.PeerExchange(rows, wl.head_dim, device)
-
-        def step():
-            xchg.step(launch.partial)
-    else:
-        dec = kd.SequenceShardDecoder(rows, wl.head_dim, world, device, partial_fn=launch.partial,
-                                      merge_fn=lambda ml, o: kvr.lse_merge(ml, o, out=out))
-
-        def step():
-            dec.step()
-
-    for _ in range(2 * ((max(args.warmup, 3) + 1) // 2)):   # an even number: the graph pairs steps
-        step()
-    torch.cuda.synchronize()
-    graph = None
-    if p2p:
-        # both steps of a pair (one per receive half) in one CUDA graph, the
-        # partial launch bound to the capture stream
-        side = torch.cuda.Stream(device)
-        launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
-                                split_tokens=args.split_tokens, stream=side.cuda_stream)
-        graph = xchg.capture_pair(launch_g.partial, side)
-        for _ in range(2):
-            xchg.replay_pair(graph)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    pairs = max(1, args.steps // 2)
-    n_steps = 2 * pairs if graph is not None else args.steps
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record()
-    if graph is not None:
-        for _ in range(pairs):
-            xchg.replay_pair(graph)
-    else:
-        for _ in range(args.steps):
-            step()
-    s1.record()
-    torch.cuda.synchronize()
-    ms = s0.elapsed_time(s1) / n_steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    lb = workloads.layer_bytes(wl)
-    step_bytes = lb["total"] * wl.layers
+    init_pg(world, device)
+    res, errors = measure_split_sequence(args, wl, world, rank, device, nccl_exchange=args.nccl_exchange)
     if rank == 0:
-        peak, peak_src = measured_peak()
-        value = step_bytes / (ms * 1e-3) / 1e9
-        line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": n_steps,
-                "warmup": args.warmup, "ms_per_step": ms, "us_per_step": ms * 1e3,
-                "tokens_per_s": wl.batch / (ms * 1e-3), "higher_is_better": True, "scaling": "strong",
+        line = {"metric": METRIC, "value": res["gbps"], "unit": "GB/s", "n_gpus": world, "steps": res["steps"],
+                "warmup": args.warmup, "ms_per_step": res["us_per_step"] / 1e3, "us_per_step": res["us_per_step"],
+                "tokens_per_s": res["tokens_per_s"], "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "u4 codes; f16/bf16 mma, fp32 accumulate and softmax",
                 "data": "synthetic (seeded N(0,1) K/V/Q, outlier key channels)",
                 "config": {"workload": wl.name, "layers": wl.layers, "global_batch": wl.batch,
-                           "seq_len": wl.seq_len, "parallelism": f"token-split x{world}",
-                           "shard_tokens": b - a, "num_splits": launch.num_splits,
-                           "exchange": ("one kernel: NVLink peer stores + signal + LSE merge" if p2p else
-                                        "NCCL all-gather + LSE merge launch" if world > 1 else "none"),
-                           "timing": ("CUDA graph of two steps (partial decode of all layers + fused exchange)"
-                                      if graph is not None else
-                                      "eager: partial decode (all layers, one launch) + exchange/merge per step")
-                                     + ", CUDA events, max over ranks"},
-                "per_gpu_fraction_of_peak": value / world / peak, "peak_source": peak_src,
-                "gpu_launches": args.steps * 2}
+                           "seq_len": wl.seq_len, "parallelism": res["parallelism"],
+                           "shard_tokens": res["shard_tokens"], "num_splits": res["num_splits"],
+                           "exchange": res["exchange"], "timing": res["timing"]},
+                "per_gpu_fraction_of_peak": res["frac_per_gpu"], "exchange_errors": errors,
+                "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]}
         print(json.dumps(line), flush=True)
-    if p2p:
-        errors = xchg.errors()
-        del graph
-        xchg.close()
-        if errors:
-            raise SystemExit(f"rank {rank}: {errors} exchange wait(s) timed out")
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    close_pg(world)
+    if errors:
+        raise SystemExit(f"{errors} exchange wait(s) timed out")
 
 
 def run_draft_loop(args, wl, world, rank, local):
-    """Speculative draft loop on the streaming cache (default workload 5):
-    rounds of `draft_steps` steps, each step appending one token to every
-    layer and decoding over it.  Times the CUDA-graph replay of a round
-    (device-side lengths, one capture) against issuing the same launches
-    eagerly; each round is rolled back to the starting length so every round
-    sees the same cache.  Per rank: its own batch (weak scaling)."""
-    import torch.distributed as dist
-
-    import kv_reduce_b200 as kvr
-    from kv_reduce_b200 import workloads
-    from kv_reduce_b200.draft import DraftLoop
-
+    """--draft-loop: the speculative draft loop (workload 5) as the whole line."""
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-    steps = max(1, wl.draft_steps or 4)
-    cache = kvr.PackedKVCache(wl.layers, wl.batch, wl.kv_heads, wl.head_dim, k_bits=wl.k_bits, v_bits=wl.v_bits,
-                              group_size=wl.group_size, residual_length=wl.residual_length,
-                              capacity=wl.seq_len + 64, device=device)
-    seed_wl = wl.scaled(seed=wl.seed + 100 * rank)
-    for i, layer in enumerate(cache.layers):
-        k, v = workloads.make_layer_kv(seed_wl, i, device=device)
-        layer.prefill(k, v)
-        del k, v
-    loop = DraftLoop(cache, q_heads=wl.q_heads, steps=steps, split_tokens=args.split_tokens)
-    g = torch.Generator(device=device).manual_seed(1234 + rank)
-    for t in (loop.q, loop.k, loop.v):
-        t.copy_(torch.randn(t.shape, generator=g, device=device).to(torch.bfloat16))
-    start = cache.get_seq_length()
-
-    def timed(fn):
-        ev = []
-        for i in range(max(args.warmup, 3) + args.steps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            cache.crop(start)
-            if i >= max(args.warmup, 3):
-                ev.append((e0, e1))
-        torch.cuda.synchronize()
-        ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
-        return max_over_ranks(ms, world, device)
-
-    graph_ms = timed(loop.replay)
-    eager_ms = timed(loop.run_eager)
-    errors = loop.errors()
-    # algorithmic bytes per draft step: the decode's bytes at the step's length
-    # plus the appended token (key row, value codes and metadata) per layer
-    step_bytes = sum(workloads.layer_bytes(wl, seq_len=start + t + 1)["total"] for t in range(steps)) / steps
-    step_bytes = step_bytes * wl.layers + wl.layers * wl.batch * wl.kv_heads * (
-        2 * wl.head_dim + wl.head_dim * wl.v_bits // 8 + 4)
-    us_step = graph_ms * 1e3 / steps
+    pg_sync = init_pg(world, device)
+    res = measure_draft_loop(args, world, rank, device, pg_sync)
     if rank == 0:
-        peak, peak_src = measured_peak()
-        line = {"metric": "draft loop: us per draft step (append + decode, all layers)", "value": us_step,
-                "unit": "us/step", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        line = {"metric": "draft loop: us per draft step (append + decode, all layers)",
+                "value": res["us_per_draft_step"], "unit": "us/step", "n_gpus": world, "steps": res["rounds"],
+                "warmup": args.warmup, "higher_is_better": False,
+                "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
                 "dtype": "u4 codes; f16/bf16 mma, fp32 accumulate and softmax",
                 "data": "synthetic (seeded N(0,1) K/V/Q, outlier key channels)",
-                "config": {"workload": wl.name, "layers": wl.layers, "batch_per_gpu": wl.batch,
-                           "seq_len": start, "draft_steps": steps, "kv_bits": f"K{wl.k_bits}V{wl.v_bits}",
-                           "timing": "CUDA graph of one round (device-side lengths) vs the same launches "
-                                     "issued eagerly; CUDA events per round, rolled back between rounds"},
-                "graph_us_per_draft_step": us_step, "eager_us_per_draft_step": eager_ms * 1e3 / steps,
-                "achieved_gbs": step_bytes / (us_step * 1e-6) / 1e9 * world,
-                "frac_of_peak_per_gpu": step_bytes / (us_step * 1e-6) / 1e9 / peak, "peak_source": peak_src,
-                "append_errors": errors,
-                # one launch per layer and draft step: the decode appends the token itself
-                "gpu_launches": args.steps * steps * wl.layers}
+                "config": {k: res[k] for k in ("workload", "layers", "global_batch", "batch_per_gpu", "seq_len",
+                                               "draft_steps", "kv_bits")},
+                "achieved_gbs": res["gbps"], "frac_of_peak_per_gpu": res["frac"],
+                "append_errors": res["append_errors"], "timing": res["timing"],
+                "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]}
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    close_pg(world)
+
+
+# ------------------------------------------------------------------- tools
+def run_engine_ab(args):
+    """Tensor cores vs CUDA cores for the packed decode attention.
+
+    The decode kernel runs its GQA-group x token tiles on the tensor cores
+    (kvr_decode_attention: mma.sync, codes as fp16 operands).  The
+    alternative is the same computation on the CUDA cores
+    (kvr_decode_attention_simt: fp32 FMA, same packed layout, split-K and LSE
+    merge, every packed byte shared by the group's query heads).  One JSON
+    line per workload and engine: all layers of a decode step, one launch per
+    32 layers, replayed as a CUDA graph, CUDA events; every workload's packed
+    cache is larger than the 126 MB L2, so no flush.
+    """
+    from kv_reduce_b200 import workloads
+    from kv_reduce_b200.packed_kv_attention import DecodeLaunch, SimtDecodeLaunch, _geometry, _layer_ptrs
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak, _ = measured_peak()
+    for key in args.configs.split(","):
+        wl = workloads.CONFIGS[key]
+        ks, vs, qs = build_cache(wl, device, 0)
+        geom = _geometry(qs[0], ks[0], vs[0])
+        step_bytes = workloads.layer_bytes(wl)["total"] * wl.layers
+        stream = torch.cuda.Stream(device)
+        first = None
+        for engine, cls in (("tensor", DecodeLaunch), ("simt", SimtDecodeLaunch)):
+            outs = [torch.empty_like(q) for q in qs]
+            ptrs = [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, outs, ks, vs)]
+            launches = [cls(geom, ptrs[i:i + 32], device, stream=stream.cuda_stream)
+                        for i in range(0, wl.layers, 32)]
+
+            def step():
+                for launch in launches:
+                    launch()
+
+            ms = time_graph(step, stream, args.steps, args.warmup, 1, torch.cuda.synchronize)
+            us = ms * 1e3 / args.steps
+            out = torch.stack(outs).float()
+            if first is None:
+                first = out
+            gbs = step_bytes / us / 1e3
+            print(json.dumps({"workload": wl.name, "engine": engine, "us_per_step": round(us, 2),
+                              "gbps": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
+                              "launches_per_step": len(launches),
+                              "max_abs_diff_vs_tensor": float((out - first).abs().max())}), flush=True)
+        del ks, vs, qs, first
+        torch.cuda.empty_cache()
+
+
+def run_all_kernels(args):
+    """Every library kernel once per round at one layer of the 32K
+    Qwen2.5-1.5B geometry (B=1, 2 KV heads, 12 query heads, D=128, K4V4,
+    group 32, residual 128), for a profiler's launch list.  The packing
+    kernels run on 8 sequences at once (134 MB of bf16 keys + values, more
+    than the 126 MB L2)."""
+    import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = workloads.CONFIGS["2"]
+    k8, v8 = workloads.make_layer_kv(wl, 0, device=dev, batch=8)
+    k1, v1 = k8[:1].contiguous(), v8[:1].contiguous()
+    q = workloads.make_query(wl, 0, device=dev)
+    for _ in range(1 + args.repeat):
+        pk8, pv8 = kvr.pack_kivi_kv(k8, v8, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+        pk8.unpack()
+        pv8.unpack()
+        pk, pv = kvr.pack_kivi_kv(k1, v1, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+        kvr.packed_kv_decode_attention(q, pk, pv)
+        layer = kvr.PackedKVCacheLayer(1, wl.kv_heads, wl.head_dim, capacity=wl.seq_len + 256, device=dev)
+        layer.prefill(k1, v1)
+        for t in range(32):
+            layer.append(k1[:, :, t:t + 1], v1[:, :, t:t + 1])
+        layer.commit()
+        rows = wl.layers * wl.q_heads
+        ml = torch.zeros(4, rows, 2, device=dev)
+        o = torch.randn(4, rows, wl.head_dim, device=dev)
+        kvr.lse_merge(ml, o)
+        codes = torch.randint(0, 16, (k8.numel(),), dtype=torch.uint8, device=dev)
+        payload = kvr.pack_unsigned(codes, 4)
+        kvr.unpack_unsigned(payload, 4, codes.numel())
+        torch.cuda.synchronize()
+        del pk8, pv8, pk, pv, layer
 
 
 def main():
     args = parse_args()
     from kv_reduce_b200 import workloads
 
+    if args.engine_ab:
+        run_engine_ab(args)
+        return
+    if args.all_kernels:
+        run_all_kernels(args)
+        return
     if args.config not in workloads.CONFIGS:
         raise SystemExit(f"unknown --config {args.config}; choose from {sorted(workloads.CONFIGS)}")
     wl = workloads.CONFIGS[args.config]

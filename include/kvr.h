@@ -222,9 +222,9 @@ int kvr_decode_attention(const kvr_decode_args* a, kvr_stream_t stream);
  * 4 MiB array compiled into the library, held by every GPU that loads it.
  * A problem whose plan needs more scratch than that returns
  * KVR_ERR_WORKSPACE.  The first call on a device looks up the array's
- * address (make it before any stream capture on that device).  Every call
- * shares the array and clears its counters; calls that overlap on the GPU
- * race.                                                                    */
+ * address (make it before any stream capture on that device); host threads
+ * may make that first call at the same time.  Every call shares the array
+ * and clears its counters; calls that overlap on the GPU race.             */
 int kvr_decode_attention_noalloc(const kvr_decode_args* a, kvr_stream_t stream);
 
 /* kvr_decode_attention with the sequence and prefix lengths read from

@@ -21,9 +21,11 @@ from .packed_kv_cache import (  # noqa: F401
 from .packed_kv_attention import (  # noqa: F401
     DecodeLaunch,
     PackedDecoder,
+    SimtDecodeLaunch,
     lse_merge,
     packed_kv_decode_attention,
     packed_kv_decode_attention_layers,
+    packed_kv_decode_attention_simt,
     theoretical_attention_flops,
 )
 from .streaming import PackedCache, PackedKVCache, PackedKVCacheLayer, PackedLayer  # noqa: F401

@@ -15,6 +15,7 @@ import torch
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("KVR_LIB", _PKG / "libkvr.so"))
+TORCH_OPS_PATH = _PKG / "libkvr_torch.so"
 
 KVR_OK = 0
 KVR_ERR_INVALID_ARGUMENT = 1
@@ -199,6 +200,26 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_simt_workspace.restype = c_size_t
     _lib = lib
     return lib
+
+
+_torch_ops = False
+
+
+def load_torch_ops() -> None:
+    """Register the C++ operators torch.ops.kvr.decode_attention /
+    decode_step / lse_merge (libkvr_torch.so over libkvr.so); raise if the
+    library has not been built."""
+    global _torch_ops
+    if _torch_ops:
+        return
+    load()
+    if not TORCH_OPS_PATH.exists():
+        raise RuntimeError(
+            f"{TORCH_OPS_PATH} is missing: build it with `python -m kv_reduce_b200.build` "
+            "(kv_reduce_b200 has no CPU fallback)"
+        )
+    torch.ops.load_library(str(TORCH_OPS_PATH))
+    _torch_ops = True
 
 
 def check(fn: str, status: int) -> None:

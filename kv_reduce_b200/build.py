@@ -17,7 +17,9 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libkvr.so"
+TORCH_LIB = PKG / "libkvr_torch.so"
 SOURCES = ["kvr_capi.cu", "kvr_pack.cu", "kvr_decode.cu", "kvr_decode_simt.cu", "kvr_exchange.cu"]
+TORCH_SOURCE = "kvr_torch.cpp"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -37,7 +39,53 @@ def _stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    """Compile every source into one shared object; returns its path."""
+    """Compile libkvr.so and the torch operator library; returns libkvr.so's path."""
+    lib = build_lib(force, verbose, ptxas_info)
+    build_torch_ops(force, verbose)
+    return lib
+
+
+def _torch_stale() -> bool:
+    if not TORCH_LIB.exists():
+        return True
+    mtime = TORCH_LIB.stat().st_mtime
+    deps = [CSRC / TORCH_SOURCE, ROOT / "include" / "kvr.h", LIB]
+    return any(p.stat().st_mtime > mtime for p in deps if p.exists())
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
+    """libkvr_torch.so: the torch.ops.kvr operators (kvr_torch.cpp, host C++
+    over libkvr.so's C ABI), compiled against this interpreter's torch."""
+    if not force and not _torch_stale():
+        return TORCH_LIB
+    import torch
+    from torch.utils import cpp_extension
+
+    cxx = os.environ.get("CXX", "g++")
+    cuda_home = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_EXTENSION_NAME=kvr_torch"]
+    for inc in cpp_extension.include_paths():
+        cmd += ["-isystem", inc]
+    cmd += ["-isystem", str(cuda_home / "include"), "-I", str(ROOT / "include"), str(CSRC / TORCH_SOURCE)]
+    for libdir in cpp_extension.library_paths():
+        cmd += ["-L", libdir, f"-Wl,-rpath,{libdir}"]
+    cmd += ["-L", str(PKG), "-lkvr", "-Wl,-rpath,$ORIGIN", "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch",
+            "-L", str(cuda_home / "lib64"), "-lcudart"]
+    tmp = TORCH_LIB.with_suffix(".so.tmp")
+    cmd += ["-o", str(tmp)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"building {TORCH_LIB.name} failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, TORCH_LIB)
+    return TORCH_LIB
+
+
+def build_lib(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
+    """Compile every CUDA source into libkvr.so; returns its path."""
     if not force and not _stale():
         return LIB
     nvcc = nvcc_path()

@@ -37,6 +37,7 @@
 #include <type_traits>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 namespace kvr {
@@ -1405,20 +1406,23 @@ namespace kvr {
 namespace dec {
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;   // 4 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-static void* g_noalloc_base[64];   // device address of the array, per device ordinal
+// Device address of the array, per device ordinal.  Host threads making
+// their first call on a device at the same time may both look it up; they
+// store the same value, and the atomic makes that race well defined.
+static std::atomic<void*> g_noalloc_base[64];
 
 static int noalloc_base(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
   if (dev < 0 || dev >= 64) return KVR_ERR_UNSUPPORTED;
-  if (!g_noalloc_base[dev]) {
-    void* p = nullptr;
+  void* p = g_noalloc_base[dev].load(std::memory_order_acquire);
+  if (!p) {
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) { set_last_cuda_error(e); return KVR_ERR_CUDA; }
-    g_noalloc_base[dev] = p;
+    g_noalloc_base[dev].store(p, std::memory_order_release);
   }
-  *out = g_noalloc_base[dev];
+  *out = p;
   return KVR_OK;
 }
 }  // namespace dec

@@ -1,10 +1,12 @@
-"""``torch.ops.kvr.*``: the packed draft-KV path as PyTorch custom operators.
+"""``torch.ops.kvr.*``: the packed draft-KV path as PyTorch operators.
 
-Each operator wraps one library launcher over plain tensors (the fields of
-the packed components) and has a fake (meta) implementation giving output
-shapes and dtypes without running anything, so code that calls the path can
-be traced by ``torch.compile`` / ``torch.export`` and captured in CUDA
-graphs with the library kernels as opaque nodes.
+The decode operators are C++ (libkvr_torch.so, ``TORCH_LIBRARY(kvr, m)`` over
+libkvr.so's C ABI): their checks, stride and pointer work and launch run
+without Python.  The packing operators are Python custom operators over the
+packing kernels.  Every operator has a fake (meta) implementation giving
+output shapes and dtypes without running anything, so code that calls the
+path can be traced by ``torch.compile`` / ``torch.export`` and captured in
+CUDA graphs with the library kernels as opaque nodes.
 
     kvr::pack_per_token(values, bits) -> (payload, scale, offset)
         packed_kv_cache.py:159-192
@@ -12,20 +14,22 @@ graphs with the library kernels as opaque nodes.
         -> (payload, scale, offset, residual)          packed_kv_cache.py:195-253
     kvr::decode_attention(query, key_payload, key_scale, key_offset,
         key_residual, value_payload, value_scale, value_offset, seq_len,
-        key_bits, value_bits, group_size, prefix_len, split_tokens) -> out
+        key_bits, value_bits, group_size, prefix_len, split_tokens=0,
+        block_tokens=32, out_fp32=False, shapes=None, layouts=3) -> out
         triton_packed_kv_attention.py:284-389
+    kvr::decode_step(query, k_new, v_new, <streaming layer buffers>, lengths,
+        geom) -> out          packed_review.py:23-31 + :78 on a streaming layer
     kvr::lse_merge(part_ml, part_o) -> out           (cross-GPU partial merge)
 
 Import this module to register them.
 """
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import Tuple
 
 import torch
 
-from .packed_kv_attention import lse_merge as _lse_merge
-from .packed_kv_attention import packed_kv_decode_attention
+from . import _lib
 from .packed_kv_cache import (
     PackedKVComponent,
     _quantized_prefix_length,
@@ -35,6 +39,26 @@ from .packed_kv_cache import (
 )
 
 Tensor = torch.Tensor
+
+_lib.load_torch_ops()
+
+
+@torch.library.register_fake("kvr::decode_attention")
+def _(query, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale, value_offset,
+      seq_len, key_bits, value_bits, group_size, prefix_len, split_tokens=0, block_tokens=32, out_fp32=False,
+      shapes=None, layouts=3):
+    return query.new_empty(query.shape, dtype=torch.float32 if out_fp32 else query.dtype)
+
+
+@torch.library.register_fake("kvr::decode_step")
+def _(query, k_new, v_new, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale,
+      value_offset, lengths, geom):
+    return query.new_empty(query.shape)
+
+
+@torch.library.register_fake("kvr::lse_merge")
+def _(part_ml, part_o):
+    return part_o.new_empty((int(part_o.shape[1]), int(part_o.shape[2])), dtype=torch.bfloat16)
 
 
 @torch.library.custom_op("kvr::pack_per_token", mutates_args=())
@@ -74,37 +98,6 @@ def _(keys: Tensor, bits: int, group_size: int, residual_length: int) -> Tuple[T
     meta = (*keys.shape[:-2], prefix // group_size, 1, head_dim)
     return (keys.new_empty(packed_num_bytes(bh * prefix * head_dim, bits), dtype=torch.uint8),
             keys.new_empty(meta, dtype=torch.bfloat16), keys.new_empty(meta, dtype=torch.bfloat16), residual)
-
-
-@torch.library.custom_op("kvr::decode_attention", mutates_args=())
-def decode_attention(query: Tensor, key_payload: Tensor, key_scale: Tensor, key_offset: Tensor,
-                     key_residual: Optional[Tensor], value_payload: Tensor, value_scale: Tensor,
-                     value_offset: Tensor, seq_len: int, key_bits: int, value_bits: int, group_size: int,
-                     prefix_len: int, split_tokens: int) -> Tensor:
-    batch, head_dim = int(query.shape[0]), int(query.shape[-1])
-    kv_heads = int(value_scale.shape[1]) if value_scale.dim() >= 3 else 1
-    shape = (batch, kv_heads, int(seq_len), head_dim)
-    k = PackedKVComponent(key_payload, key_scale, key_offset, key_residual, shape, int(key_bits),
-                          "per_channel_grouped_affine", query.dtype, int(group_size), int(prefix_len))
-    v = PackedKVComponent(value_payload, value_scale, value_offset, None, shape, int(value_bits),
-                          "per_token_affine", query.dtype)
-    return packed_kv_decode_attention(query, k, v, split_tokens=split_tokens)
-
-
-@decode_attention.register_fake
-def _(query, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale, value_offset,
-      seq_len, key_bits, value_bits, group_size, prefix_len, split_tokens):
-    return torch.empty_like(query)
-
-
-@torch.library.custom_op("kvr::lse_merge", mutates_args=())
-def lse_merge(part_ml: Tensor, part_o: Tensor) -> Tensor:
-    return _lse_merge(part_ml, part_o)
-
-
-@lse_merge.register_fake
-def _(part_ml: Tensor, part_o: Tensor) -> Tensor:
-    return part_o.new_empty((int(part_o.shape[1]), int(part_o.shape[2])), dtype=torch.bfloat16)
 
 
 def decode_attention_from(query: Tensor, packed_keys: PackedKVComponent, packed_values: PackedKVComponent, *,

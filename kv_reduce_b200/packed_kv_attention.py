@@ -3,7 +3,8 @@ kv_reduce/triton_packed_kv_attention.py on sm_100a.
 
 ``packed_kv_decode_attention`` keeps the reference signature, argument
 meaning and ``ValueError`` preconditions (triton_packed_kv_attention.py:284-314)
-and runs one CUDA launch (split-K decode + fused LSE merge) from libkvr.so.
+and runs one CUDA launch (split-K decode + fused LSE merge) from libkvr.so,
+through the C++ operator torch.ops.kvr.decode_attention (libkvr_torch.so).
 
 Differences from the reference, stated where a caller could notice them:
   * bits: {2, 4, 8} are accepted (the reference: {4, 8});
@@ -18,7 +19,6 @@ Differences from the reference, stated where a caller could notice them:
 from __future__ import annotations
 
 import ctypes
-import threading
 from dataclasses import dataclass
 from typing import Dict, List, Sequence, Tuple
 
@@ -147,7 +147,6 @@ def _layer_ptrs(query: torch.Tensor | None, out: torch.Tensor | None, k: PackedK
 # split-partial workspace is scratch that stream-ordered launches can share
 # the same way.  A launch object keeps references to the buffers it was
 # built with, so growing a cached buffer never frees memory still in use.
-_tls = threading.local()
 _COUNTERS: Dict[Tuple[int, int], torch.Tensor] = {}
 _WORKSPACE: Dict[Tuple[int, int], torch.Tensor] = {}
 _PLANS: Dict[tuple, Tuple[int, int, int]] = {}
@@ -241,6 +240,26 @@ class DecodeLaunch:
             self.args, self.token_begin, self.token_end, part_ml.data_ptr(), part_o.data_ptr(), self.stream))
 
 
+class SimtDecodeLaunch(DecodeLaunch):
+    """A prepared decode launch on the CUDA-core engine
+    (kvr_decode_attention_simt: fp32 FMA instead of tensor cores, same
+    packed layout, split-K and LSE merge).  It is the measured alternative
+    to the tensor-core kernel, kept as a library entry point so the A/B
+    (``bench.py --engine-ab``) runs against a tested implementation."""
+
+    def __init__(self, geom: CacheGeometry, layers: Sequence[_lib.LayerPtrs], device: torch.device,
+                 split_tokens: int = 0, stream: int | None = None, out_fp32: bool = False) -> None:
+        super().__init__(geom, layers, device, split_tokens=split_tokens, stream=stream, out_fp32=out_fp32)
+        n = int(_lib.load().kvr_decode_simt_workspace(self.args))
+        if n == 0:
+            raise ValueError("this geometry is not supported by the CUDA-core engine")
+        self.simt_workspace = torch.empty(n, dtype=torch.uint8, device=device)
+        self.args.workspace, self.args.workspace_bytes = self.simt_workspace.data_ptr(), n
+
+    def __call__(self) -> None:
+        _lib.check("kvr_decode_attention_simt", _lib.load().kvr_decode_attention_simt(self.args, self.stream))
+
+
 def _effective_split(split_tokens: int, block_tokens: int) -> int:
     if split_tokens <= 0:
         return 0
@@ -261,29 +280,54 @@ def packed_kv_decode_attention(
     Drop-in for triton_packed_kv_attention.packed_kv_decode_attention
     (:284-389): returns a tensor like ``query``.  ``out_dtype=torch.float32``
     (an addition) returns the fp32 result before the cast to the query dtype.
+    The checks (the reference's, same order and messages), the stride and
+    pointer work and the launch run in C++ (torch.ops.kvr.decode_attention).
     """
-    _validate(query, packed_keys, packed_values, block_tokens)
+    if out_dtype not in (None, query.dtype, torch.float32):
+        raise ValueError("out_dtype must be None, the query dtype or torch.float32.")
+    k, v = packed_keys, packed_values
+    ks, vs = k.shape, v.shape
+    if len(ks) != 4 or len(vs) != 4:
+        _validate(query, k, v, block_tokens)   # raises the reference's error for this input
+    if _decode_op is None:
+        _bind_ops()
+    layouts = (k.layout == "per_channel_grouped_affine") | ((v.layout == "per_token_affine") << 1)
+    return _decode_op(query, k.payload, k.scale, k.offset, k.residual, v.payload, v.scale, v.offset, ks[2],
+                      k.bits, v.bits, k.group_size, k.prefix_length, split_tokens, block_tokens,
+                      out_dtype == torch.float32, (*ks, *vs), layouts)
+
+
+_decode_op = None
+
+
+def _bind_ops() -> None:
+    global _decode_op
+    _lib.load_torch_ops()
+    _decode_op = torch.ops.kvr.decode_attention.default
+
+
+def packed_kv_decode_attention_simt(
+    query: torch.Tensor,
+    packed_keys: PackedKVComponent,
+    packed_values: PackedKVComponent,
+    *,
+    split_tokens: int = 0,
+    out_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """packed_kv_decode_attention computed by the CUDA-core engine (fp32 FMA).
+
+    Same arguments, preconditions and result (to fp32 rounding) as the
+    tensor-core path; geometries the engine does not cover raise ValueError.
+    """
+    _validate(query, packed_keys, packed_values, 32)
     if out_dtype not in (None, query.dtype, torch.float32):
         raise ValueError("out_dtype must be None, the query dtype or torch.float32.")
     query = query.contiguous()
     geom = _geometry(query, packed_keys, packed_values)
     out_fp32 = out_dtype == torch.float32
     out = torch.empty_like(query, dtype=torch.float32) if out_fp32 else torch.empty_like(query)
-    layer = _layer_ptrs(query, out, packed_keys, packed_values)
-    split = _effective_split(split_tokens, block_tokens)
-    stream = _lib.stream_ptr(query.device)
-    # one prepared launch per shape and stream, per host thread (the library
-    # call releases the GIL, so threads must not share an argument block)
-    cache = _tls.__dict__.setdefault("launches", {})
-    key = (geom, split, stream, out_fp32)
-    launch = cache.get(key)
-    if launch is None:
-        if len(cache) >= 64:
-            cache.clear()
-        launch = cache[key] = DecodeLaunch(geom, [layer], query.device, split_tokens=split, stream=stream,
-                                           out_fp32=out_fp32)
-    else:
-        launch.layers[0] = layer
+    launch = SimtDecodeLaunch(geom, [_layer_ptrs(query, out, packed_keys, packed_values)], query.device,
+                              split_tokens=_effective_split(split_tokens, 32), out_fp32=out_fp32)
     launch()
     return out
 

@@ -34,6 +34,17 @@ def _round_up(x: int, m: int) -> int:
     return -(-x // m) * m
 
 
+_step_op = None
+_step_out_op = None
+
+
+def _bind_ops() -> None:
+    global _step_op, _step_out_op
+    _lib.load_torch_ops()
+    _step_op = torch.ops.kvr.decode_step.default
+    _step_out_op = torch.ops.kvr.decode_step.out
+
+
 class PackedKVCacheLayer:
     """One layer of the preallocated packed cache."""
 
@@ -246,7 +257,8 @@ class PackedKVCacheLayer:
                     out: torch.Tensor | None = None) -> torch.Tensor:
         """append(k, v) then attention(query): for one new token a single
         decode launch that stores the token before attending
-        (kvr_decode_step), else an append and a decode call.
+        (kvr_decode_step, through the C++ operator torch.ops.kvr.decode_step),
+        else an append and a decode call.
 
         Both forms read the lengths from the layer's device-side copy and
         move it on themselves, so the host only rewrites the query,
@@ -257,6 +269,23 @@ class PackedKVCacheLayer:
         hold across commits.
         """
         n = int(k.shape[2]) if k.dim() == 4 else -1
+        if (n == 1 and self.seq_len > 0 and self.seq_len < self.capacity
+                and self.seq_len - self.prefix_len < self.cap_residual):
+            # one token, room in the buffers: the C++ operator checks the
+            # tensors and launches the fused append + decode
+            self.pin_residual = True
+            geom = (self.capacity, self.cap_prefix, self.cap_residual, self.k_bits, self.v_bits, self.group_size,
+                    int(split_tokens))
+            bufs = (self.key_payload, self.key_scale, self.key_offset, self.key_residual[self._cur],
+                    self.value_payload, self.value_scale, self.value_offset, self.device_lengths())
+            if _step_op is None:
+                _bind_ops()
+            if out is None:
+                out = _step_op(query, k, v, *bufs, geom)
+            else:
+                _step_out_op(query, k, v, *bufs, geom, out=out)
+            self.seq_len += 1
+            return out
         if (k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or k.shape != v.shape or n < 1
                 or tuple(k.shape[:2]) != (self.batch, self.kv_heads) or k.shape[3] != self.head_dim):
             raise ValueError(f"k/v must be bf16 [{self.batch}, {self.kv_heads}, n, {self.head_dim}].")

@@ -1,8 +1,8 @@
 """Generate golden vectors by running the reference's own packed_kv_cache.py.
 
-Run in a container where the reference checkout exists:
+Run where a checkout of the reference exists, giving its path:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the KV_Reduce checkout>
 
 It imports kv_reduce.packed_kv_cache from that checkout (read-only), runs it
 on seeded bf16 inputs -- including the exact inputs of the reference's own
@@ -130,4 +130,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path of the KV_Reduce checkout>")
+    main(sys.argv[1])

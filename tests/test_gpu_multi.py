@@ -1,8 +1,15 @@
-"""Sequence split across 2 GPUs with the fused NVLink exchange + merge kernel
-(kvr_exchange_merge) against the single-GPU decode of the whole sequence.
-Runs only where at least two GPUs are visible."""
+"""The sequence split's fused NVLink exchange + merge kernel (kvr_exchange_merge).
+
+On one GPU: the kernel's time-limited wait for a peer that never signals
+runs out, sets the error flag and returns, and the next step completes.
+On two GPUs (skipped with fewer): the split against the single-GPU decode of
+the whole sequence, eagerly and as the replayed CUDA graph the benchmark
+times, at the benchmarked 28-layer 32K shape.
+"""
+import ctypes
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -16,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result):
+def _worker(rank, world, port, result, seq_len, layers, graph_steps):
     import torch.distributed as dist
 
     import kv_reduce_b200 as kvr
@@ -31,7 +38,7 @@ def _worker(rank, world, port, result):
 
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=device)
     try:
-        wl = workloads.CONFIGS["2"].scaled(seq_len=5000, layers=3)
+        wl = workloads.CONFIGS["2"].scaled(seq_len=seq_len, layers=layers)
         a, b = kd.token_shards(wl.seq_len, world, align=wl.group_size)[rank]
         ks, vs, qs, full = [], [], [], []
         for layer in range(wl.layers):
@@ -52,6 +59,17 @@ def _worker(rank, world, port, result):
             out = xchg.step(launch.partial).float()
             torch.cuda.synchronize()
             worst = max(worst, float((out - ref).abs().max()))
+        if graph_steps:
+            # the benchmark's form: both steps of a pair in one CUDA graph
+            side = torch.cuda.Stream(device)
+            launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)],
+                                    device, stream=side.cuda_stream)
+            graph = xchg.capture_pair(launch_g.partial, side)
+            for _ in range(graph_steps):
+                xchg.replay_pair(graph)
+                torch.cuda.synchronize()
+                worst = max(worst, float((xchg.out.float() - ref).abs().max()))
+            del graph
         errors = xchg.errors()
         xchg.close()
         result[rank] = (worst, errors, float(ref.abs().max()))
@@ -60,15 +78,82 @@ def _worker(rank, world, port, result):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpu_sequence_split_fused_exchange(built_lib):
+@pytest.mark.parametrize("seq_len,layers,graph_steps", [(5000, 3, 0), (32768, 28, 3)])
+def test_two_gpu_sequence_split_fused_exchange(built_lib, seq_len, layers, graph_steps):
     import torch.multiprocessing as mp
 
     world = 2
     with mp.get_context("spawn").Manager() as manager:
         result = manager.dict()
-        mp.spawn(_worker, args=(world, _free_port(), result), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), result, seq_len, layers, graph_steps), nprocs=world,
+                 join=True)
         for rank in range(world):
             worst, errors, scale = result[rank]
             assert errors == 0
             # bf16 output of the merge vs the fp32 single-GPU result
             assert worst <= 2e-3 + scale * 2.0 ** -8, (rank, worst)
+
+
+def test_exchange_wait_times_out_without_peer(built_lib):
+    """World 2 emulated on one GPU: both receive buffers are local and only
+    rank 0 runs, so its wait for rank 1's signal has nothing to end it but
+    the 50 ms limit.  The kernel must return, raise the error flag, still
+    have pushed its own partials and signal to the peer's buffer, and the
+    next step -- with the peer's signal and an empty partial in place --
+    must complete without error and equal rank 0's partial normalised."""
+    from kv_reduce_b200 import _lib
+
+    lib = _lib.load()
+    world, rows, D = 2, 24, 128
+    slot = rows * (2 + D)
+    data_floats = 2 * world * slot
+    bufs = [torch.zeros(data_floats + 64, dtype=torch.float32, device="cuda") for _ in range(world)]
+    recv = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    signal = recv + data_floats * 4
+    state = torch.zeros(4, dtype=torch.int32, device="cuda")     # epoch, counter, error
+    out = torch.empty(rows, D, dtype=torch.bfloat16, device="cuda")
+    st = state.data_ptr()
+    args = _lib.ExchangeArgs(world, 0, rows, D, recv.data_ptr(), signal.data_ptr(), st, st + 4, st + 8,
+                             out.data_ptr(), 50_000_000)
+    g = torch.Generator(device="cuda").manual_seed(11)
+
+    def view(buf, parity, src):
+        base = (parity * world + src) * slot
+        return buf[base:base + 2 * rows].view(rows, 2), buf[base + 2 * rows:base + slot].view(rows, D)
+
+    def fill_partial(parity):
+        ml, o = view(bufs[0], parity, 0)
+        ml[:, 0] = torch.randn(rows, generator=g, device="cuda")
+        ml[:, 1] = torch.rand(rows, generator=g, device="cuda") + 0.5
+        o.copy_(torch.randn(rows, D, generator=g, device="cuda"))
+        return ml, o
+
+    stream = torch.cuda.current_stream().cuda_stream
+    fill_partial(1)                       # step 1 (epoch 1) uses receive half 1
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert lib.kvr_exchange_merge(ctypes.byref(args), stream) == _lib.KVR_OK
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert state[2].item() == 1, "the time-out did not raise the error flag"
+    assert state[0].item() == 1 and state[1].item() == 0
+    assert 0.04 <= waited < 5.0, waited
+    ml1, o1 = view(bufs[0], 1, 0)
+    pml, po = view(bufs[1], 1, 0)          # rank 0's slot in the peer's buffer
+    assert torch.equal(pml, ml1) and torch.equal(po, o1)
+    assert bufs[1].view(torch.int32)[data_floats].item() == 1    # rank 0 signalled epoch 1 to the peer
+
+    # step 2: the peer has arrived with an empty partial (no tokens)
+    state[2] = 0
+    ml, o = fill_partial(0)
+    eml, eo = view(bufs[0], 0, 1)
+    eml[:, 0] = float("-inf")
+    eml[:, 1] = 0.0
+    eo.zero_()
+    bufs[0].view(torch.int32)[data_floats + 1] = 2                 # rank 1's signal for epoch 2
+    torch.cuda.synchronize()
+    assert lib.kvr_exchange_merge(ctypes.byref(args), stream) == _lib.KVR_OK
+    torch.cuda.synchronize()
+    assert state[2].item() == 0 and state[0].item() == 2
+    expect = o / ml[:, 1:2]
+    assert torch.allclose(out.float(), expect, rtol=2.0 ** -8, atol=1e-6)

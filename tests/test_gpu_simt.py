@@ -26,20 +26,16 @@ def kvr(built_lib):
 ])
 @pytest.mark.parametrize("split", [0, 64])
 def test_simt_matches_oracle(kvr, shape, hq, kb, vb, split):
-    from kv_reduce_b200.engine_ab import simt_decode
-
     k, v, q = make(shape, hq, kb, vb, 32, 128, seed=shape[2] + kb)
     pk, pv = kvr.pack_kivi_kv(k, v, k_bits=kb, v_bits=vb, group_size=32, residual_length=128)
-    out = simt_decode(q, pk, pv, split_tokens=split, out_dtype=torch.float32)
+    out = kvr.packed_kv_decode_attention_simt(q, pk, pv, split_tokens=split, out_dtype=torch.float32)
     check(out, oracle_out(k, v, q, kb, vb, 32, 128), f"simt {shape} K{kb}V{vb} split {split}")
     tensor = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=split, out_dtype=torch.float32)
     assert (out - tensor).abs().max().item() <= 2e-3
 
 
 def test_simt_rejects_unsupported_geometry(kvr):
-    from kv_reduce_b200.engine_ab import simt_decode
-
     k, v, q = make((1, 2, 300, 128), 12, 8, 8, 32, 128, seed=5)
     pk, pv = kvr.pack_kivi_kv(k, v, k_bits=8, v_bits=8, group_size=32, residual_length=128)
     with pytest.raises(ValueError):
-        simt_decode(q, pk, pv)
+        kvr.packed_kv_decode_attention_simt(q, pk, pv)
