@@ -26,8 +26,10 @@ headline (weak scaling, batch sharding, no collective on the data path); the
 step time is the max over ranks.  At N > 1 the line also carries
 `split_sequence`: ONE batch-1 32K sequence with its tokens split across the
 ranks (partial decode + the fused NVLink exchange and LSE merge kernel).
-``--impl reference`` times the reference's unfused CPU path (unpack + SDPA,
-restated in oracle/cpu_baseline.py) on the host cores.
+``--impl reference`` times the reference's unfused CPU path (unpack + SDPA)
+on the host cores: the reference's own code from its install under
+baseline/_ref, or its restatement in oracle/cpu_baseline.py when that is
+absent.
 
 Tools on the same workloads (not part of the driver's line):
   --engine-ab     tensor cores vs CUDA cores for the decode (one JSON line per
@@ -178,30 +180,60 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_baseline_sample(wl, seconds: float, layer_bytes: int):
-    """Reference unfused path (unpack K, unpack V, SDPA) on host cores, one
-    32K-token layer repeated for about `seconds`."""
+REF_DIR = ROOT / "baseline" / "_ref"   # the reference package, installed offline (pip --target)
+
+
+def reference_cpu_step(wl):
+    """One step of the reference's unfused decode on host cores for one
+    layer of `wl`: (kind, step function, description).
+
+    kind "reference": the reference's own code, imported from its install
+    under baseline/_ref -- pack_kivi_kv once (kv_reduce/packed_kv_cache.py:256-275),
+    then per step gqa_attention(query, packed_keys.unpack(), packed_values.unpack())
+    (kv_reduce/experiments/benchmark_packed_kv_attention.py:58-76, :236-240).
+    kind "port": the same operator sequence restated by oracle/cpu_baseline.py
+    (pinned to the reference's outputs), when the install is absent."""
     import numpy as np
 
     from kv_reduce_b200 import workloads
-    from oracle import cpu_baseline
 
-    torch.set_num_threads(os.cpu_count() or 1)
     k, v = workloads.make_layer_kv(wl, 0, device="cpu")
     q = workloads.make_query(wl, 0, device="cpu")
+    if (REF_DIR / "kv_reduce" / "packed_kv_cache.py").exists():
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        from kv_reduce.experiments.benchmark_packed_kv_attention import gqa_attention
+        from kv_reduce.packed_kv_cache import pack_kivi_kv
+
+        pk, pv = pack_kivi_kv(k, v, k_bits=wl.k_bits, v_bits=wl.v_bits, group_size=wl.group_size,
+                              residual_length=wl.residual_length)
+        return ("reference", lambda: gqa_attention(q, pk.unpack(), pv.unpack()),
+                "the reference's own PackedKVComponent.unpack() x2 + gqa_attention (SDPA, bf16), "
+                "kv_reduce installed under baseline/_ref")
+    from oracle import cpu_baseline
+
     bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
     pk, pv = cpu_baseline.pack_cpu(bits(k), bits(v), wl.k_bits, wl.v_bits, wl.group_size, wl.residual_length)
-    cpu_baseline.unfused_decode(q, pk, pv)   # warm-up
+    return ("port", lambda: cpu_baseline.unfused_decode(q, pk, pv),
+            "unpack + SDPA in bf16, the reference's unfused path restated by the oracle port")
+
+
+def cpu_baseline_sample(wl, seconds: float, layer_bytes: int):
+    """Reference unfused path (unpack K, unpack V, SDPA) on host cores, one
+    layer repeated for about `seconds`."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    kind, step, what = reference_cpu_step(wl)
+    step()   # warm-up
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_baseline.unfused_decode(q, pk, pv)
+        step()
         n += 1
         if time.perf_counter() - t0 >= seconds:
             break
     dt = (time.perf_counter() - t0) / n
     return {"value": layer_bytes / dt / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"{n} x one {wl.seq_len}-token layer of the {wl.name} workload (unpack + SDPA, bf16)",
+            "kind": kind,
+            "sample": f"{n} x one {wl.seq_len}-token layer of the {wl.name} workload ({what})",
             "ms_per_layer": dt * 1e3, "ms_per_step_extrapolated": dt * 1e3 * wl.layers}
 
 
@@ -226,25 +258,17 @@ def run_reference(args, wl, world, rank):
         return
     lb = workloads.layer_bytes(wl)["total"]
     torch.set_num_threads(os.cpu_count() or 1)
-    import numpy as np
-
-    from oracle import cpu_baseline
-
-    k, v = workloads.make_layer_kv(wl, 0, device="cpu")
-    q = workloads.make_query(wl, 0, device="cpu")
-    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
-    pk, pv = cpu_baseline.pack_cpu(bits(k), bits(v), wl.k_bits, wl.v_bits, wl.group_size, wl.residual_length)
+    kind, step, what = reference_cpu_step(wl)
     for _ in range(args.warmup):
-        cpu_baseline.unfused_decode(q, pk, pv)
+        step()
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        cpu_baseline.unfused_decode(q, pk, pv)
+        step()
         times.append(time.perf_counter() - t0)
     dt = sum(times) / len(times)
     value = lb / dt / 1e9
-    sample = (f"one {wl.seq_len}-token layer per step (of {wl.layers}), unpack + SDPA in bf16 on host cores, "
-              f"the reference's unfused path restated by the oracle port")
+    sample = f"one {wl.seq_len}-token layer per step (of {wl.layers}), {what}"
     line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1e3 * wl.layers,
             "ms_per_step_note": "extrapolated: layer time x layers",
@@ -252,7 +276,7 @@ def run_reference(args, wl, world, rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "impl": "reference",
             "config": workload_config(wl, world, args),
-            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": kind,
                              "sample": sample},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
