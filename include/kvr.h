@@ -189,6 +189,14 @@ typedef struct {
   const uint16_t* value_offset;
   const uint16_t* query;
   void* out;            /* bf16 or fp32, see kvr_decode_args.out_dtype */
+  /* Optional, NULL to leave it out: key_scale as fp16 pairs in the decode
+   * kernel's register order, written from key_scale by kvr_key_scale_pairs
+   * (same shape and strides as key_scale).  Given it, the decode reads these
+   * pairs in place of the bf16 scales (the same number of bytes) instead of
+   * converting every group's scales for each query head; the output is
+   * bit-identical.  Zero-initialise the struct so the field is NULL when
+   * unused.                                                                */
+  const uint16_t* key_scale_pairs;
 } kvr_layer_ptrs;
 
 typedef struct {
@@ -207,6 +215,21 @@ typedef struct {
   void* workspace; size_t workspace_bytes;   /* split partials */
   int* counters;      /* n_layers*batch*kv_heads ints, zero on entry */
 } kvr_decode_args;
+
+/* Key scales as fp16 pairs in the decode kernel's register order, for
+ * kvr_layer_ptrs.key_scale_pairs.  No reference counterpart: a decode
+ * lookup table derived from the stored bf16 scales
+ * (packed_kv_cache.py:232-246), written once per key group when the
+ * group is packed (pack_per_channel_grouped_affine, PackedLayer.commit).
+ * Converts groups [group0, group0 + groups) of every (b,h) slab; `pairs`
+ * has key_scale's layout ([bh][groups][D] 16-bit words, the given
+ * bh stride).  head_dim in {64, 128}, key_bits in {2, 4, 8}.              */
+typedef struct {
+  const uint16_t* scale; int64_t scale_bh_stride;   /* bf16, elements */
+  uint16_t* pairs; int64_t pairs_bh_stride;         /* fp16 pairs, elements */
+  int bh, groups, group0, head_dim, key_bits;
+} kvr_scale_pairs_args;
+int kvr_key_scale_pairs(const kvr_scale_pairs_args* a, kvr_stream_t stream);
 
 /* Fills the split count, workspace bytes and counter count for `a`
  * (workspace and counters ignored). */

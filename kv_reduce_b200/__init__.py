@@ -10,6 +10,7 @@ All compute runs in libkvr.so (CUDA C++ for sm_100a, C ABI in include/kvr.h).
 from .packed_kv_cache import (  # noqa: F401
     FULL_PRECISION_BITS,
     PackedKVComponent,
+    key_scale_pairs,
     pack_kivi_kv,
     pack_per_channel_grouped_affine,
     pack_per_token_affine,

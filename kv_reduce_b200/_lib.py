@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "kvr_set_lengths",
     "kvr_decode_attention_lengths",
     "kvr_decode_step",
+    "kvr_key_scale_pairs",
     "kvr_exchange_merge",
     "kvr_exchange_alloc",
     "kvr_exchange_open",
@@ -126,6 +127,15 @@ class LayerPtrs(Structure):
         ("key_payload", c_void_p), ("key_scale", c_void_p), ("key_offset", c_void_p),
         ("key_residual", c_void_p), ("value_payload", c_void_p), ("value_scale", c_void_p),
         ("value_offset", c_void_p), ("query", c_void_p), ("out", c_void_p),
+        ("key_scale_pairs", c_void_p),
+    ]
+
+
+class ScalePairsArgs(Structure):
+    _fields_ = [
+        ("scale", c_void_p), ("scale_bh_stride", c_int64),
+        ("pairs", c_void_p), ("pairs_bh_stride", c_int64),
+        ("bh", c_int), ("groups", c_int), ("group0", c_int), ("head_dim", c_int), ("key_bits", c_int),
     ]
 
 
@@ -189,6 +199,7 @@ def load() -> ctypes.CDLL:
     lib.kvr_set_lengths.argtypes = [c_void_p, c_int, c_int, c_void_p]
     lib.kvr_decode_attention_lengths.argtypes = [POINTER(DecodeArgs), c_void_p, c_int, c_void_p]
     lib.kvr_decode_step.argtypes = [POINTER(DecodeArgs), c_void_p, c_void_p, c_void_p, c_int, c_void_p]
+    lib.kvr_key_scale_pairs.argtypes = [POINTER(ScalePairsArgs), c_void_p]
     lib.kvr_exchange_merge.argtypes = [POINTER(ExchangeArgs), c_void_p]
     lib.kvr_exchange_alloc.argtypes = [c_size_t, POINTER(c_void_p), ctypes.c_char_p]
     lib.kvr_exchange_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]

@@ -61,7 +61,7 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
     import torch
     from torch.utils import cpp_extension
 
-    cxx = os.environ.get("CXX", "g++")
+    cxx = host_cxx()
     cuda_home = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
@@ -80,8 +80,30 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"building {TORCH_LIB.name} failed:\n{res.stdout}\n{res.stderr}")
+    _check_shared_cxx_runtime(tmp)
     os.replace(tmp, TORCH_LIB)
     return TORCH_LIB
+
+
+def host_cxx() -> str:
+    """The C++ compiler for the torch operator library: KVR_CXX if set, else
+    the system g++.  $CXX is not used, because a compiler wrapper that links
+    libstdc++ statically would give the library its own C++ runtime: a
+    TORCH_CHECK exception thrown there is then caught by torch's runtime and
+    the process crashes."""
+    for cand in (os.environ.get("KVR_CXX"), "/usr/bin/g++", shutil.which("g++")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("g++ not found; set KVR_CXX to the C++ compiler torch was built with")
+
+
+def _check_shared_cxx_runtime(lib: Path) -> None:
+    """The operator library must use the shared libstdc++ that torch uses
+    (see host_cxx)."""
+    res = subprocess.run(["readelf", "-d", str(lib)], capture_output=True, text=True)
+    if res.returncode == 0 and "libstdc++.so" not in res.stdout:
+        raise RuntimeError(f"{lib.name} does not link the shared libstdc++ (statically linked C++ runtime); "
+                           "build it with the system g++ (KVR_CXX)")
 
 
 def build_lib(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:

@@ -249,10 +249,12 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 // Exact product split in fp16x2 (TwoProduct with a fused multiply-add):
 // hi = fl(a*b), lo = fma(a, b, -hi); hi + lo == a*b exactly unless the
-// error term falls into the fp16 subnormal range.
+// error term falls into the fp16 subnormal range.  -hi is a floating-point
+// negate, which the compiler folds into the fma's operand.
 __device__ __forceinline__ void two_prod_h2(uint32_t a, uint32_t b, uint32_t& hi, uint32_t& lo) {
   asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(hi) : "r"(a), "r"(b));
-  const uint32_t nhi = hi ^ 0x80008000u;
+  uint32_t nhi;
+  asm("neg.f16x2 %0, %1;\n" : "=r"(nhi) : "r"(hi));
   asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(lo) : "r"(a), "r"(b), "r"(nhi));
 }
 

@@ -15,18 +15,20 @@
 //           (code bits in the mantissa of a zero exponent: c * f * 2^-24);
 //           the per-channel key scale is folded into the query,
 //           q~ = (q / f) * s_g (f = the code's bit-position factor), carried
-//           as an exact fp16 hi + lo pair (TwoProduct); the zero point enters
-//           as a per-group bias q . z_g from a bf16 mma; scores are scaled by
-//           2^24 * log2e / sqrt(D) after the mma.
+//           as an exact fp16 hi + lo pair (TwoProduct); s_g comes as fp16
+//           pairs in register order from a table written when the group was
+//           packed (kvr_key_scale_pairs), or is converted from the bf16
+//           scales per chunk when a cache has no table; the zero point
+//           enters as a per-group bias q . z_g from a bf16 mma; scores are
+//           scaled by 2^24 * log2e / sqrt(D) after the mma.
 //   softmax = fp32 online softmax in log2 units with warp-shuffle reductions.
 //   P V    = mma.sync with M = head dim, N = heads, K = 16 tokens: P moves
 //           from accumulator to operand layout with movmatrix.trans, value
-//           codes arrive token-paired through ldmatrix.trans, become fp16 by
-//           the 0x6400 magic-exponent method (code | 0x6400 is 1024 + code)
-//           and are centred (n - 2^(b-1)) by the same subtraction, the
-//           per-token value scale is folded into P
-//           (P~ = p * s_t) and the zero point is accumulated as
-//           sum p * (z_t + 2^(b-1) s_t) in fp32.
+//           codes arrive token-paired through ldmatrix.trans and become
+//           exact fp16 subnormals with one AND, as the keys do
+//           (c * f * 2^-24, undone in the epilogue), the per-token value
+//           scale is folded into P (P~ = p * s_t) and the zero point is
+//           accumulated as sum p * z_t in fp32.
 //   BF16 residual window = same pass, bf16 mma of raw keys against the raw
 //           bf16 query (exact products).
 //   epilogue = CTA merge of the 4 warps in shared memory, then a two-level
@@ -104,6 +106,7 @@ struct LayerPtrs {
   const uint16_t* vo;
   const uint16_t* q;
   void* out;
+  const uint16_t* ksp;   // key scales as fp16 pairs in register order, or null
 };
 
 template <int MAXL>
@@ -260,7 +263,7 @@ struct GroupQ {
 // bias lands in the accumulator layout of the QK^T tiles.
 template <int D, int KB>
 __device__ __forceinline__ void group_query(GroupQ<D>& gq, const uint4* qs, const uint16_t* meta, int lane,
-                                            int dbase) {
+                                            int dbase, bool pairs) {
   uint32_t sw[D / 8];
 #pragma unroll
   for (int v = 0; v < D / 32; ++v) {
@@ -277,7 +280,7 @@ __device__ __forceinline__ void group_query(GroupQ<D>& gq, const uint4* qs, cons
       const int d0 = key_dlocal<KB>(r, 0), d1 = key_dlocal<KB>(r, 1);
       const float s0 = (d0 & 1) ? bf16hi(sw[d0 >> 1]) : bf16lo(sw[d0 >> 1]);
       const float s1 = (d1 & 1) ? bf16hi(sw[d1 >> 1]) : bf16lo(sw[d1 >> 1]);
-      two_prod_h2(qw[k], pack_half2(s0, s1), gq.hi[r], gq.lo[r]);
+      two_prod_h2(qw[k], pairs ? sw[r] : pack_half2(s0, s1), gq.hi[r], gq.lo[r]);
     }
   }
   float bf[4] = {0.f, 0.f, 0.f, 0.f};
@@ -334,7 +337,7 @@ __device__ __forceinline__ void group_bias(float (&bf)[4], const uint4* qs, cons
 // g+24 in kw[0..3]; the hi/lo query for each k-step is formed on the fly
 // from shared memory (s words and q/f words in windows), keeping the live
 // register set small.  h0/h1 arrive holding the bias.
-template <int D, int KB>
+template <int D, int KB, bool PAIRS>
 __device__ __forceinline__ void qk_chunk(float (&h0)[4], float (&l0)[4], float (&h1)[4], float (&l1)[4],
                                          const uint32_t (&kw)[4][D / 8 / (2 * (8 / KB))], const uint4* qs,
                                          const uint16_t* meta, int lane, int dbase) {
@@ -359,11 +362,17 @@ __device__ __forceinline__ void qk_chunk(float (&h0)[4], float (&l0)[4], float (
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int r = 2 * js + k;
-      const int d0 = key_dlocal<KB>(r, 0), d1 = key_dlocal<KB>(r, 1);
-      const int w0 = (d0 >> 1) - base, w1 = (d1 >> 1) - base;
-      const float s0 = (d0 & 1) ? bf16hi(sw[w0]) : bf16lo(sw[w0]);
-      const float s1 = (d1 & 1) ? bf16hi(sw[w1]) : bf16lo(sw[w1]);
-      two_prod_h2(qw[r - base], pack_half2(s0, s1), bh[k], bl[k]);
+      uint32_t sp;
+      if constexpr (PAIRS) {
+        sp = sw[r - base];   // the pair of register r, converted when the group was packed
+      } else {
+        const int d0 = key_dlocal<KB>(r, 0), d1 = key_dlocal<KB>(r, 1);
+        const int w0 = (d0 >> 1) - base, w1 = (d1 >> 1) - base;
+        const float s0 = (d0 & 1) ? bf16hi(sw[w0]) : bf16lo(sw[w0]);
+        const float s1 = (d1 & 1) ? bf16hi(sw[w1]) : bf16lo(sw[w1]);
+        sp = pack_half2(s0, s1);
+      }
+      two_prod_h2(qw[r - base], sp, bh[k], bl[k]);
     }
     const int r0 = 2 * js, r1 = 2 * js + 1;
     const uint32_t a0 = key_codes_h2<KB>(kw[0][r0 / RPW], r0 % RPW);
@@ -456,7 +465,10 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     const LayerPtrs& Lp = p.L[layer];
     const int b = bh / p.HKV, kvh = bh % p.HKV;
     const uint8_t* kp = Lp.kp + (int64_t)bh * p.kp_bh;
-    const uint16_t* ksc = Lp.ks + (int64_t)bh * p.km_bh;
+    // key scales: the fp16 pair table when the cache has one (same layout
+    // and bytes as the bf16 scales), else the bf16 scales, converted per chunk
+    const bool pairs = Lp.ksp != nullptr;
+    const uint16_t* ksc = (pairs ? Lp.ksp : Lp.ks) + (int64_t)bh * p.km_bh;
     const uint16_t* kof = Lp.ko + (int64_t)bh * p.km_bh;
     const uint16_t* kres = Lp.kr + (int64_t)bh * p.kr_bh;
     const uint8_t* vp = Lp.vp + (int64_t)bh * p.vp_bh;
@@ -637,8 +649,9 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
 
       // A full prefix chunk inside one key group (the common case) runs a
       // body free of row bounds logic; other chunks take the general body.
-      auto chunk_body = [&](auto full_c) {
+      auto chunk_body = [&](auto full_c, auto pairs_c) {
         constexpr bool FULL = decltype(full_c)::value;
+        constexpr bool PAIRS = decltype(pairs_c)::value;   // FULL body only
         // ------------------------------------------------------------ Q K^T
         float sc[2][4];
         if constexpr (FULL) {
@@ -653,7 +666,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
           for (int k = 0; k < 4; ++k) bf[k] *= kKeyScale;
           float h0[4] = {bf[0], bf[1], bf[2], bf[3]}, l0[4] = {0.f, 0.f, 0.f, 0.f};
           float h1[4] = {bf[0], bf[1], bf[2], bf[3]}, l1[4] = {0.f, 0.f, 0.f, 0.f};
-          qk_chunk<D, KB>(h0, l0, h1, l1, kw, qs, meta0, lane, dbase);
+          qk_chunk<D, KB, PAIRS>(h0, l0, h1, l1, kw, qs, meta0, lane, dbase);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             sc[0][k] = (h0[k] + l0[k]) * cs_k;
@@ -669,7 +682,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
               const int grp = mtok >> log2G;
               const int slot = (mt == 1 && grp != (tok0 >> log2G)) ? 1 : 0;
               GroupQ<D> gq;
-              group_query<D, KB>(gq, qs, meta0 + slot * (C::META / 2), lane, dbase);
+              group_query<D, KB>(gq, qs, meta0 + slot * (C::META / 2), lane, dbase, pairs);
               uint32_t kw0[C::NWK], kw1[C::NWK];
               load_key_row<D, KB>(kw0, st + C::K_OFF, 16 * mt + g, t4);
               load_key_row<D, KB>(kw1, st + C::K_OFF, 16 * mt + g + 8, t4);
@@ -746,7 +759,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         uint32_t pb[2][2];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
-          // token scale s and centred offset z + 2^(vb-1) s of rows g, g+8
+          // token scale s and offset z of rows g, g+8
           uint32_t w_lo, w_hi;
           if (p.vm_staged) {
             const uint16_t* vm = reinterpret_cast<const uint16_t*>(st + C::VM_OFF);
@@ -771,8 +784,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
             w_hi = __shfl_sync(0xffffffffu, vm_cur, 16 * mt + g + 8);
           }
           const float s_lo = bf16lo(w_lo), s_hi = bf16lo(w_hi);
-          const float z_lo = fmaf(s_lo, (float)(1 << (VB - 1)), bf16hi(w_lo));
-          const float z_hi = fmaf(s_hi, (float)(1 << (VB - 1)), bf16hi(w_hi));
+          const float z_lo = bf16hi(w_lo), z_hi = bf16hi(w_hi);
           float pr[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) pr[k] = fast_exp2(sc[mt][k] - m_run[k & 1]);   // -inf -> 0
@@ -809,16 +821,20 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
 #pragma unroll
           for (int mi = 0; mi < C::KS; ++mi) {
             const int ra = 2 * mi, rb = 2 * mi + 1;
-            const uint32_t a0 = codes_to_h2<VB, true>(vx[0][ra / C::CPB_V], ra % C::CPB_V);
-            const uint32_t a1 = codes_to_h2<VB, true>(vx[0][rb / C::CPB_V], rb % C::CPB_V);
-            const uint32_t a2 = codes_to_h2<VB, true>(vx[1][ra / C::CPB_V], ra % C::CPB_V);
-            const uint32_t a3 = codes_to_h2<VB, true>(vx[1][rb / C::CPB_V], rb % C::CPB_V);
+            const uint32_t a0 = key_codes_h2<VB>(vx[0][ra / C::CPB_V], ra % C::CPB_V);
+            const uint32_t a1 = key_codes_h2<VB>(vx[0][rb / C::CPB_V], rb % C::CPB_V);
+            const uint32_t a2 = key_codes_h2<VB>(vx[1][ra / C::CPB_V], ra % C::CPB_V);
+            const uint32_t a3 = key_codes_h2<VB>(vx[1][rb / C::CPB_V], rb % C::CPB_V);
             mma_f16(acc[mi], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
           }
         }
       };
-      if ((n_valid == kChunk) && (tok0 + kChunk <= P) && (log2G >= 5)) chunk_body(std::true_type{});
-      else chunk_body(std::false_type{});
+      if ((n_valid == kChunk) && (tok0 + kChunk <= P) && (log2G >= 5)) {
+        if (pairs) chunk_body(std::true_type{}, std::true_type{});
+        else chunk_body(std::true_type{}, std::false_type{});
+      } else {
+        chunk_body(std::false_type{}, std::false_type{});
+      }
       __syncwarp();
       stage = stage + 1 == kStages ? 0 : stage + 1;
     }
@@ -848,7 +864,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         const int r = 2 * mi + hh;
         const int cch = r / C::CPB_V, j = r % C::CPB_V;
         const int d = cch * (128 / VB) + g * C::CPB_V + j;
-        const float inv = 1.f / code_factor<VB>(j);
+        const float inv = kKeyUnscale / code_factor<VB>(j);   // value codes carry f * 2^-24
 #pragma unroll
         for (int e = 0; e < 2; ++e)
           mO[(warp * kHeads + 2 * t4 + e) * D + d] = fmaf(acc[mi][2 * hh + e], inv, z_run[e]);
@@ -1143,7 +1159,8 @@ static int validate(const kvr_decode_args* a) {
     if (a->prefix_len < a->seq_len && !L.key_residual) return KVR_ERR_INVALID_ARGUMENT;
     if ((L.key_payload && !aligned16(L.key_payload)) || !aligned16(L.value_payload) ||
         (L.key_scale && !aligned16(L.key_scale)) || (L.key_offset && !aligned16(L.key_offset)) ||
-        (L.key_residual && !aligned16(L.key_residual)) || !aligned16(L.query) || !aligned16(L.out))
+        (L.key_residual && !aligned16(L.key_residual)) || !aligned16(L.query) || !aligned16(L.out) ||
+        (L.key_scale_pairs && !aligned16(L.key_scale_pairs)))
       return KVR_ERR_MISALIGNED;
   }
   return KVR_OK;
@@ -1154,7 +1171,7 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   for (int l = 0; l < a->n_layers; ++l) {
     const kvr_layer_ptrs& L = a->layers[l];
     p.L[l] = LayerPtrs{L.key_payload, L.key_scale, L.key_offset, L.key_residual, L.value_payload,
-                       L.value_scale, L.value_offset, L.query, L.out};
+                       L.value_scale, L.value_offset, L.query, L.out, L.key_scale_pairs};
   }
   p.n_layers = a->n_layers;
   p.BH = a->batch * a->kv_heads;
@@ -1382,6 +1399,53 @@ extern "C" int kvr_decode_partial(const kvr_decode_args* a, int token_begin, int
                                   float* part_o, kvr_stream_t stream) {
   if (!a || !part_ml || !part_o) return KVR_ERR_INVALID_ARGUMENT;
   return dec::run(a, token_begin, token_end, part_ml, part_o, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Key scales as fp16 pairs in the decode kernel's register order
+// (kvr_layer_ptrs.key_scale_pairs).  Word w = t4 * D/8 + r of a group holds
+// the scales of the two channels key register r of lane slice t4 covers,
+// dbase + key_dlocal(r, 0) and dbase + key_dlocal(r, 1) (dbase = t4 * D/4),
+// rounded to fp16 exactly as the decode kernel rounds them (cvt.rn from the
+// bf16 value), so a decode reading the table equals one converting per chunk.
+namespace kvr {
+namespace dec {
+template <int D, int KB>
+__global__ void __launch_bounds__(256) scale_pairs_kernel(const kvr_scale_pairs_args a) {
+  constexpr int W = D / 2;   // 32-bit words per group
+  const int64_t n = (int64_t)a.bh * a.groups * W;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % W);
+    const int64_t rest = i / W;
+    const int64_t grp = a.group0 + rest % a.groups;
+    const int64_t bh = rest / a.groups;
+    const int t4 = w / (D / 8), r = w % (D / 8);
+    const int d0 = t4 * (D / 4) + key_dlocal<KB>(r, 0), d1 = t4 * (D / 4) + key_dlocal<KB>(r, 1);
+    const uint16_t* s = a.scale + bh * a.scale_bh_stride + grp * D;
+    const uint32_t word = pack_half2(bf16_bits_to_f32(s[d0]), bf16_bits_to_f32(s[d1]));
+    *reinterpret_cast<uint32_t*>(a.pairs + bh * a.pairs_bh_stride + grp * D + 2 * w) = word;
+  }
+}
+}  // namespace dec
+}  // namespace kvr
+
+extern "C" int kvr_key_scale_pairs(const kvr_scale_pairs_args* a, kvr_stream_t stream) {
+  if (!a || !a->scale || !a->pairs || a->bh < 0 || a->groups < 0 || a->group0 < 0) return KVR_ERR_INVALID_ARGUMENT;
+  if (a->head_dim != 64 && a->head_dim != 128) return KVR_ERR_UNSUPPORTED;
+  if (a->key_bits != 2 && a->key_bits != 4 && a->key_bits != 8) return KVR_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(a->pairs) & 3u) || (a->pairs_bh_stride & 1)) return KVR_ERR_MISALIGNED;
+  const int64_t n = (int64_t)a->bh * a->groups * (a->head_dim / 2);
+  if (n == 0) return KVR_OK;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  cudaStream_t s = as_stream(stream);
+#define KVR_PAIRS(D_, KB_)                                                        \
+  if (a->head_dim == D_ && a->key_bits == KB_) {                                  \
+    dec::scale_pairs_kernel<D_, KB_><<<blocks, 256, 0, s>>>(*a);                   \
+    return check_launch();                                                        \
+  }
+  KVR_PAIRS(128, 2) KVR_PAIRS(128, 4) KVR_PAIRS(128, 8) KVR_PAIRS(64, 2) KVR_PAIRS(64, 4) KVR_PAIRS(64, 8)
+#undef KVR_PAIRS
+  return KVR_ERR_UNSUPPORTED;
 }
 
 // ---------------------------------------------------------------------------

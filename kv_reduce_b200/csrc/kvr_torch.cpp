@@ -120,7 +120,8 @@ at::Tensor decode_attention(const at::Tensor& query, const at::Tensor& key_paylo
                             const std::optional<at::Tensor>& value_scale,
                             const std::optional<at::Tensor>& value_offset, int64_t seq_len, int64_t kb, int64_t vb,
                             int64_t G, int64_t P, int64_t split, int64_t block, bool out_fp32,
-                            at::OptionalIntArrayRef shapes, int64_t layouts) {
+                            at::OptionalIntArrayRef shapes, int64_t layouts,
+                            const std::optional<at::Tensor>& key_scale_pairs) {
   // the reference's preconditions, in its order (:293-314)
   TORCH_CHECK_VALUE(query.is_cuda(), "Packed attention requires a CUDA query tensor.");
   TORCH_CHECK_VALUE(query.dim() == 4 && query.size(2) == 1, "query must have shape [batch, query_heads, 1, head_dim].");
@@ -166,6 +167,13 @@ at::Tensor decode_attention(const at::Tensor& query, const at::Tensor& key_paylo
   check_on(key_residual, dev);
   check_on(value_scale, dev);
   check_on(value_offset, dev);
+  check_on(key_scale_pairs, dev);
+  // the fp16 scale pairs are used only when laid out like the bf16 scales
+  const void* pairs = nullptr;
+  if (key_scale_pairs.has_value() && key_scale_pairs->defined() && key_scale_pairs->numel() > 0 &&
+      key_scale_pairs->element_size() == 2 && key_scale_pairs->sizes() == key_scale->sizes() &&
+      key_scale_pairs->strides() == key_scale->strides())
+    pairs = key_scale_pairs->data_ptr();
 
   kvr_decode_args a;
   std::memset(&a, 0, sizeof(a));
@@ -197,6 +205,7 @@ at::Tensor decode_attention(const at::Tensor& query, const at::Tensor& key_paylo
   L.value_offset = static_cast<const uint16_t*>(ptr_or_null(value_offset));
   L.query = static_cast<const uint16_t*>(q.data_ptr());
   L.out = out.data_ptr();
+  L.key_scale_pairs = static_cast<const uint16_t*>(pairs);
   a.layers = &L;
   a.n_layers = 1;
   a.batch = (int)B;
@@ -222,14 +231,15 @@ at::Tensor decode_attention(const at::Tensor& query, const at::Tensor& key_paylo
 // live in `lengths` (int32[4] on the device) and advance on the device.
 // geom = [capacity, prefix_capacity, residual_capacity, key_bits, value_bits,
 //         group_size, split_tokens]
-at::Tensor& decode_step_out(const at::Tensor& query, const at::Tensor& k_new, const at::Tensor& v_new,
-                            const at::Tensor& key_payload, const at::Tensor& key_scale, const at::Tensor& key_offset,
-                            const at::Tensor& key_residual, const at::Tensor& value_payload,
-                            const at::Tensor& value_scale, const at::Tensor& value_offset, const at::Tensor& lengths,
-                            at::IntArrayRef geom, at::Tensor& out) {
+//
+// Every argument check runs in check_step, before anything is allocated:
+// decode_step raises its ValueError with no output tensor alive.
+void check_step(const at::Tensor& query, const at::Tensor& k_new, const at::Tensor& v_new,
+                const at::Tensor& key_payload, const at::Tensor& key_scale, const at::Tensor& key_offset,
+                const at::Tensor& key_residual, const at::Tensor& value_payload, const at::Tensor& value_scale,
+                const at::Tensor& value_offset, const at::Tensor& lengths, at::IntArrayRef geom,
+                const std::optional<at::Tensor>& key_scale_pairs) {
   TORCH_CHECK_VALUE(geom.size() == 7, "kvr::decode_step: geom must hold 7 integers.");
-  const int64_t cap = geom[0], cap_prefix = geom[1], cap_res = geom[2], kb = geom[3], vb = geom[4], G = geom[5],
-                split = geom[6];
   TORCH_CHECK_VALUE(query.is_cuda() && query.dim() == 4 && query.size(2) == 1 &&
                         query.scalar_type() == at::kBFloat16,
                     "query must be a bf16 CUDA tensor [batch, q_heads, 1, head_dim].");
@@ -242,16 +252,36 @@ at::Tensor& decode_step_out(const at::Tensor& query, const at::Tensor& k_new, co
                         k_new.size(1) == HKV && k_new.size(2) == 1 && k_new.size(3) == D,
                     "k/v must be bf16 [", B, ", ", HKV, ", 1, ", D, "].");
   const at::Device dev = query.device();
-  for (const at::Tensor* t : {&k_new, &v_new, &key_payload, &key_scale, &key_offset, &key_residual, &value_payload,
-                              &value_scale, &value_offset, &lengths})
+  const at::Tensor* tensors[] = {&k_new,   &v_new,         &key_payload, &key_scale,    &key_offset,
+                                 &key_residual, &value_payload, &value_scale, &value_offset, &lengths};
+  for (const at::Tensor* t : tensors)
     TORCH_CHECK_VALUE(t->is_cuda() && t->device() == dev, "All tensors must be on the query's CUDA device.");
   TORCH_CHECK_VALUE(lengths.scalar_type() == at::kInt && lengths.numel() >= 4 && lengths.is_contiguous(),
                     "lengths must be a contiguous int32[4] device tensor.");
+  if (key_scale_pairs.has_value() && key_scale_pairs->defined())
+    TORCH_CHECK_VALUE(key_scale_pairs->is_cuda() && key_scale_pairs->device() == dev &&
+                          key_scale_pairs->element_size() == 2 && key_scale_pairs->sizes() == key_scale.sizes() &&
+                          key_scale_pairs->strides() == key_scale.strides(),
+                      "key_scale_pairs must be laid out like key_scale on the query's device.");
+}
+
+at::Tensor& decode_step_out(const at::Tensor& query, const at::Tensor& k_new, const at::Tensor& v_new,
+                            const at::Tensor& key_payload, const at::Tensor& key_scale, const at::Tensor& key_offset,
+                            const at::Tensor& key_residual, const at::Tensor& value_payload,
+                            const at::Tensor& value_scale, const at::Tensor& value_offset, const at::Tensor& lengths,
+                            at::IntArrayRef geom, const std::optional<at::Tensor>& key_scale_pairs,
+                            at::Tensor& out) {
+  check_step(query, k_new, v_new, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale,
+             value_offset, lengths, geom, key_scale_pairs);
+  TORCH_CHECK_VALUE(out.sizes() == query.sizes() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
+                        out.device() == query.device(),
+                    "out must be a contiguous bf16 tensor like the query.");
+  const int64_t cap = geom[0], cap_prefix = geom[1], cap_res = geom[2], kb = geom[3], vb = geom[4], G = geom[5],
+                split = geom[6];
+  const int64_t B = value_payload.size(0), HKV = value_payload.size(1), D = query.size(3);
+  const at::Device dev = query.device();
   c10::cuda::CUDAGuard guard(dev);
   const at::Tensor q = query.contiguous(), k = k_new.contiguous(), v = v_new.contiguous();
-  TORCH_CHECK_VALUE(out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
-                        out.device() == dev,
-                    "out must be a contiguous bf16 tensor like the query.");
   kvr_layer_ptrs L;
   L.key_payload = static_cast<const uint8_t*>(key_payload.data_ptr());
   L.key_scale = static_cast<const uint16_t*>(key_scale.data_ptr());
@@ -262,6 +292,9 @@ at::Tensor& decode_step_out(const at::Tensor& query, const at::Tensor& k_new, co
   L.value_offset = static_cast<const uint16_t*>(value_offset.data_ptr());
   L.query = static_cast<const uint16_t*>(q.data_ptr());
   L.out = out.data_ptr();
+  L.key_scale_pairs = (key_scale_pairs.has_value() && key_scale_pairs->defined() && key_scale_pairs->numel() > 0)
+                          ? static_cast<const uint16_t*>(key_scale_pairs->data_ptr())
+                          : nullptr;
   kvr_decode_args a;
   std::memset(&a, 0, sizeof(a));
   a.layers = &L;
@@ -293,12 +326,13 @@ at::Tensor& decode_step_out(const at::Tensor& query, const at::Tensor& k_new, co
 at::Tensor decode_step(const at::Tensor& query, const at::Tensor& k_new, const at::Tensor& v_new,
                        const at::Tensor& key_payload, const at::Tensor& key_scale, const at::Tensor& key_offset,
                        const at::Tensor& key_residual, const at::Tensor& value_payload, const at::Tensor& value_scale,
-                       const at::Tensor& value_offset, const at::Tensor& lengths, at::IntArrayRef geom) {
-  TORCH_CHECK_VALUE(query.is_cuda() && query.scalar_type() == at::kBFloat16,
-                    "query must be a bf16 CUDA tensor [batch, q_heads, 1, head_dim].");
+                       const at::Tensor& value_offset, const at::Tensor& lengths, at::IntArrayRef geom,
+                       const std::optional<at::Tensor>& key_scale_pairs) {
+  check_step(query, k_new, v_new, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale,
+             value_offset, lengths, geom, key_scale_pairs);
   at::Tensor out = at::empty(query.sizes(), query.options().memory_format(at::MemoryFormat::Contiguous));
   decode_step_out(query, k_new, v_new, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale,
-                  value_offset, lengths, geom, out);
+                  value_offset, lengths, geom, key_scale_pairs, out);
   return out;
 }
 
@@ -325,13 +359,14 @@ TORCH_LIBRARY(kvr, m) {
   m.def("decode_attention(Tensor query, Tensor key_payload, Tensor? key_scale, Tensor? key_offset, "
         "Tensor? key_residual, Tensor value_payload, Tensor? value_scale, Tensor? value_offset, int seq_len, "
         "int key_bits, int value_bits, int group_size, int prefix_len, int split_tokens=0, int block_tokens=32, "
-        "bool out_fp32=False, int[]? shapes=None, int layouts=3) -> Tensor");
+        "bool out_fp32=False, int[]? shapes=None, int layouts=3, Tensor? key_scale_pairs=None) -> Tensor");
   m.def("decode_step(Tensor query, Tensor k_new, Tensor v_new, Tensor key_payload, Tensor key_scale, "
         "Tensor key_offset, Tensor(a!) key_residual, Tensor(b!) value_payload, Tensor(c!) value_scale, "
-        "Tensor(d!) value_offset, Tensor(e!) lengths, int[] geom) -> Tensor");
+        "Tensor(d!) value_offset, Tensor(e!) lengths, int[] geom, Tensor? key_scale_pairs=None) -> Tensor");
   m.def("decode_step.out(Tensor query, Tensor k_new, Tensor v_new, Tensor key_payload, Tensor key_scale, "
         "Tensor key_offset, Tensor(a!) key_residual, Tensor(b!) value_payload, Tensor(c!) value_scale, "
-        "Tensor(d!) value_offset, Tensor(e!) lengths, int[] geom, *, Tensor(f!) out) -> Tensor(f!)");
+        "Tensor(d!) value_offset, Tensor(e!) lengths, int[] geom, Tensor? key_scale_pairs=None, *, "
+        "Tensor(f!) out) -> Tensor(f!)");
   m.def("lse_merge(Tensor part_ml, Tensor part_o) -> Tensor");
 }
 

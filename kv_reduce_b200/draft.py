@@ -64,7 +64,8 @@ class DraftLoop:
                              layer.value_payload.stride(1), layer.value_scale.stride(1))
         ptrs = _lib.LayerPtrs(layer.key_payload.data_ptr(), layer.key_scale.data_ptr(), layer.key_offset.data_ptr(),
                               res.data_ptr(), layer.value_payload.data_ptr(), layer.value_scale.data_ptr(),
-                              layer.value_offset.data_ptr(), q.data_ptr(), out.data_ptr())
+                              layer.value_offset.data_ptr(), q.data_ptr(), out.data_ptr(),
+                              _lib.ptr(layer.key_scale_pairs))
         return DecodeLaunch(geom, [ptrs], layer.device, split_tokens=self.split_tokens, stream=stream)
 
     def _append_args(self, layer: PackedKVCacheLayer, k: torch.Tensor, v: torch.Tensor) -> _lib.AppendArgs:

@@ -15,10 +15,11 @@ CUDA graphs with the library kernels as opaque nodes.
     kvr::decode_attention(query, key_payload, key_scale, key_offset,
         key_residual, value_payload, value_scale, value_offset, seq_len,
         key_bits, value_bits, group_size, prefix_len, split_tokens=0,
-        block_tokens=32, out_fp32=False, shapes=None, layouts=3) -> out
-        triton_packed_kv_attention.py:284-389
+        block_tokens=32, out_fp32=False, shapes=None, layouts=3,
+        key_scale_pairs=None) -> out                   triton_packed_kv_attention.py:284-389
     kvr::decode_step(query, k_new, v_new, <streaming layer buffers>, lengths,
-        geom) -> out          packed_review.py:23-31 + :78 on a streaming layer
+        geom, key_scale_pairs=None) -> out
+                              packed_review.py:23-31 + :78 on a streaming layer
     kvr::lse_merge(part_ml, part_o) -> out           (cross-GPU partial merge)
 
 Import this module to register them.
@@ -30,6 +31,7 @@ from typing import Tuple
 import torch
 
 from . import _lib
+from .packed_kv_attention import scale_pairs_of
 from .packed_kv_cache import (
     PackedKVComponent,
     _quantized_prefix_length,
@@ -46,13 +48,13 @@ _lib.load_torch_ops()
 @torch.library.register_fake("kvr::decode_attention")
 def _(query, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale, value_offset,
       seq_len, key_bits, value_bits, group_size, prefix_len, split_tokens=0, block_tokens=32, out_fp32=False,
-      shapes=None, layouts=3):
+      shapes=None, layouts=3, key_scale_pairs=None):
     return query.new_empty(query.shape, dtype=torch.float32 if out_fp32 else query.dtype)
 
 
 @torch.library.register_fake("kvr::decode_step")
 def _(query, k_new, v_new, key_payload, key_scale, key_offset, key_residual, value_payload, value_scale,
-      value_offset, lengths, geom):
+      value_offset, lengths, geom, key_scale_pairs=None):
     return query.new_empty(query.shape)
 
 
@@ -107,4 +109,4 @@ def decode_attention_from(query: Tensor, packed_keys: PackedKVComponent, packed_
         query, packed_keys.payload, packed_keys.scale, packed_keys.offset, packed_keys.residual,
         packed_values.payload, packed_values.scale, packed_values.offset, int(packed_keys.shape[-2]),
         int(packed_keys.bits), int(packed_values.bits), int(packed_keys.group_size),
-        int(packed_keys.prefix_length), int(split_tokens))
+        int(packed_keys.prefix_length), int(split_tokens), key_scale_pairs=scale_pairs_of(packed_keys))

@@ -125,7 +125,7 @@ def _geometry(query: torch.Tensor, k: PackedKVComponent, v: PackedKVComponent) -
 def _check_device(dev_index: int, k: PackedKVComponent, v: PackedKVComponent) -> None:
     """Every cache tensor must live on the query's GPU (the kernel reads them
     through device pointers; a host tensor's address would be read as one)."""
-    for t in (k.payload, k.scale, k.offset, k.residual, v.payload, v.scale, v.offset):
+    for t in (k.payload, k.scale, k.offset, k.residual, k.scale_pairs, v.payload, v.scale, v.offset):
         if t is not None and (not t.is_cuda or t.get_device() != dev_index):
             raise ValueError("Packed K/V tensors must be on the query's CUDA device.")
 
@@ -139,7 +139,17 @@ def _layer_ptrs(query: torch.Tensor | None, out: torch.Tensor | None, k: PackedK
         _lib.ptr(k.payload), _lib.ptr(k.scale), _lib.ptr(k.offset), _lib.ptr(res),
         _lib.ptr(v.payload), _lib.ptr(v.scale), _lib.ptr(v.offset),
         query.data_ptr() if query is not None else None, out.data_ptr() if out is not None else None,
+        _lib.ptr(scale_pairs_of(k)),
     )
+
+
+def scale_pairs_of(k: PackedKVComponent) -> torch.Tensor | None:
+    """The component's key-scale pair table when it matches its scales'
+    shape and strides (the decode indexes both alike), else None."""
+    t = k.scale_pairs
+    if t is None or k.scale is None or t.shape != k.scale.shape or t.stride() != k.scale.stride():
+        return None
+    return t
 
 
 # Split-merge counters: zero on entry, left zero by every completed launch,
@@ -294,7 +304,7 @@ def packed_kv_decode_attention(
     layouts = (k.layout == "per_channel_grouped_affine") | ((v.layout == "per_token_affine") << 1)
     return _decode_op(query, k.payload, k.scale, k.offset, k.residual, v.payload, v.scale, v.offset, ks[2],
                       k.bits, v.bits, k.group_size, k.prefix_length, split_tokens, block_tokens,
-                      out_dtype == torch.float32, (*ks, *vs), layouts)
+                      out_dtype == torch.float32, (*ks, *vs), layouts, scale_pairs_of(k))
 
 
 _decode_op = None

@@ -119,6 +119,11 @@ class PackedKVComponent:
     output_dtype: torch.dtype
     group_size: int = 0
     prefix_length: int = 0
+    # Keys only, optional: the scales as fp16 pairs in the decode kernel's
+    # register order (key_scale_pairs), a lookup table derived from `scale`
+    # when the group is packed.  Not part of the reference's record and not
+    # counted in its byte properties; the decode reads it in place of `scale`.
+    scale_pairs: torch.Tensor | None = None
 
     @property
     def payload_bytes(self) -> int:
@@ -240,6 +245,31 @@ def pack_per_token_affine(
     )
 
 
+def key_scale_pairs(scale: torch.Tensor, bits: int, *, out: torch.Tensor | None = None, group0: int = 0,
+                    groups: int | None = None) -> torch.Tensor | None:
+    """fp16 pairs of the key scales in the decode kernel's register order
+    (kvr_key_scale_pairs): a tensor with ``scale``'s layout ([..., groups, 1,
+    D] 16-bit words), or ``out`` with groups [group0, group0 + groups)
+    filled.  None when the decode kernel does not cover the geometry
+    (head_dim outside {64, 128} or bits outside {2, 4, 8})."""
+    D = int(scale.shape[-1]) if scale.dim() else 0
+    if D not in (64, 128) or bits not in (2, 4, 8) or scale.dim() < 3 or scale.numel() == 0:
+        return None
+    if out is None:
+        out = torch.empty(scale.shape, dtype=torch.int16, device=scale.device)
+    n_groups = int(scale.shape[-3])
+    bh = scale.numel() // (n_groups * D)
+    sb = n_groups * D if scale.is_contiguous() else int(scale.stride(-4))
+    ob = int(out.shape[-3]) * D if out.is_contiguous() else int(out.stride(-4))
+    a = _lib.ScalePairsArgs()
+    a.scale, a.scale_bh_stride = scale.data_ptr(), sb
+    a.pairs, a.pairs_bh_stride = out.data_ptr(), ob
+    a.bh, a.groups, a.group0 = bh, n_groups - group0 if groups is None else int(groups), int(group0)
+    a.head_dim, a.key_bits = D, int(bits)
+    _lib.call("kvr_key_scale_pairs", a, _lib.stream_ptr(scale.device))
+    return out
+
+
 def pack_per_channel_grouped_affine(
     keys: torch.Tensor,
     bits: int,
@@ -291,7 +321,7 @@ def pack_per_channel_grouped_affine(
     return PackedKVComponent(
         payload=payload, scale=scale, offset=offset, residual=residual, shape=tuple(keys.shape),
         bits=bits, layout="per_channel_grouped_affine", output_dtype=keys.dtype,
-        group_size=group_size, prefix_length=prefix_length,
+        group_size=group_size, prefix_length=prefix_length, scale_pairs=key_scale_pairs(scale, bits),
     )
 
 

@@ -27,7 +27,7 @@ import torch
 
 from . import _lib
 from .packed_kv_attention import packed_kv_decode_attention
-from .packed_kv_cache import PackedKVComponent, _quantized_prefix_length, tensor_bytes
+from .packed_kv_cache import PackedKVComponent, _quantized_prefix_length, key_scale_pairs, tensor_bytes
 
 
 def _round_up(x: int, m: int) -> int:
@@ -80,6 +80,9 @@ class PackedKVCacheLayer:
         self.key_payload = torch.zeros(B, H, cap_p, D * self.k_bits // 8, dtype=torch.uint8, device=dev)
         self.key_scale = torch.zeros(B, H, max(cap_p // G, 1), 1, D, dtype=torch.bfloat16, device=dev)
         self.key_offset = torch.zeros_like(self.key_scale)
+        # the decode's fp16 scale pairs (key_scale_pairs), kept in step with key_scale
+        self.key_scale_pairs = (torch.zeros(self.key_scale.shape, dtype=torch.int16, device=dev)
+                                if D in (64, 128) and self.k_bits in (2, 4, 8) else None)
         self.key_residual = [torch.zeros(B, H, cap_r, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
         self.value_payload = torch.zeros(B, H, capacity, D * self.v_bits // 8, dtype=torch.uint8, device=dev)
         self.value_scale = torch.zeros(B, H, capacity, 1, dtype=torch.bfloat16, device=dev)
@@ -87,7 +90,7 @@ class PackedKVCacheLayer:
 
     def _grow(self, need_seq: int, need_res: int) -> None:
         old = (self.key_payload, self.key_scale, self.key_offset, self.key_residual[self._cur],
-               self.value_payload, self.value_scale, self.value_offset)
+               self.value_payload, self.value_scale, self.value_offset, self.key_scale_pairs)
         S, P, R = self.seq_len, self.prefix_len, self.seq_len - self.prefix_len
         cap = self.capacity
         while cap < need_seq:
@@ -102,6 +105,8 @@ class PackedKVCacheLayer:
         self.key_payload[:, :, :P].copy_(old[0][:, :, :P])
         self.key_scale[:, :, :P // G].copy_(old[1][:, :, :P // G])
         self.key_offset[:, :, :P // G].copy_(old[2][:, :, :P // G])
+        if self.key_scale_pairs is not None:
+            self.key_scale_pairs[:, :, :P // G].copy_(old[7][:, :, :P // G])
         self.key_residual[0][:, :, :R].copy_(old[3][:, :, :R])
         self.value_payload[:, :, :S].copy_(old[4][:, :, :S])
         self.value_scale[:, :, :S].copy_(old[5][:, :, :S])
@@ -141,6 +146,7 @@ class PackedKVCacheLayer:
             a.meta_bh_stride = self.key_scale.stride(1)
             a.bh, a.groups, a.group0, a.group_size, a.head_dim, a.bits = bh, P // G, 0, G, D, self.k_bits
             _lib.call("kvr_quantize_grouped", a, self._stream())
+            self._pairs(0, P // G)
         self._cur = 0
         self.key_residual[0][:, :, :S - P].copy_(keys[:, :, P:])
         if S > 0:
@@ -195,6 +201,7 @@ class PackedKVCacheLayer:
         a.prefix_len, a.prefix_capacity = self.prefix_len, self.cap_prefix
         a.group_size, a.head_dim, a.key_bits = self.group_size, self.head_dim, self.k_bits
         _lib.call("kvr_flush_groups", a, self._stream())
+        self._pairs(self.prefix_len // self.group_size, promoted // self.group_size)
         self.prefix_len += promoted
         if self.pin_residual:
             rest = res_len - promoted
@@ -203,6 +210,11 @@ class PackedKVCacheLayer:
             self._cur = 1 - self._cur
         self._sync_lengths()
         return promoted
+
+    def _pairs(self, group0: int, groups: int) -> None:
+        """Refresh the scale pair table for key groups [group0, group0 + groups)."""
+        if self.key_scale_pairs is not None and groups > 0:
+            key_scale_pairs(self.key_scale, self.k_bits, out=self.key_scale_pairs, group0=group0, groups=groups)
 
     def crop(self, length: int) -> None:
         """Roll back to `length` tokens inside the uncommitted tail."""
@@ -238,6 +250,7 @@ class PackedKVCacheLayer:
             offset=self.key_offset[:, :, :P // G], residual=self.key_residual[self._cur][:, :, :S - P],
             shape=(B, H, S, D), bits=self.k_bits, layout="per_channel_grouped_affine",
             output_dtype=torch.bfloat16, group_size=G, prefix_length=P,
+            scale_pairs=None if self.key_scale_pairs is None else self.key_scale_pairs[:, :, :P // G],
         )
 
     @property
@@ -281,9 +294,9 @@ class PackedKVCacheLayer:
             if _step_op is None:
                 _bind_ops()
             if out is None:
-                out = _step_op(query, k, v, *bufs, geom)
+                out = _step_op(query, k, v, *bufs, geom, self.key_scale_pairs)
             else:
-                _step_out_op(query, k, v, *bufs, geom, out=out)
+                _step_out_op(query, k, v, *bufs, geom, self.key_scale_pairs, out=out)
             self.seq_len += 1
             return out
         if (k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or k.shape != v.shape or n < 1
@@ -342,7 +355,8 @@ class PackedKVCacheLayer:
                              self.value_scale.stride(1))
         ptrs = _lib.LayerPtrs(self.key_payload.data_ptr(), self.key_scale.data_ptr(), self.key_offset.data_ptr(),
                               res.data_ptr(), self.value_payload.data_ptr(), self.value_scale.data_ptr(),
-                              self.value_offset.data_ptr(), query.data_ptr(), out.data_ptr())
+                              self.value_offset.data_ptr(), query.data_ptr(), out.data_ptr(),
+                              _lib.ptr(self.key_scale_pairs))
         return a, DecodeLaunch(geom, [ptrs], self.device, split_tokens=split_tokens, stream=stream)
 
     def breakdown(self) -> Dict[str, int]:

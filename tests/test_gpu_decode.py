@@ -333,3 +333,68 @@ def test_cache_on_another_device_is_rejected(kvr):
         kvr.packed_kv_decode_attention(q, pk, cpu_v)
     with pytest.raises(ValueError):
         kvr.PackedDecoder([pk], [cpu_v], q_heads=12)
+
+
+def _key_dlocal(kb, r, e):
+    rpw = 2 * (8 // kb)
+    return (r // rpw) * (32 // kb) + r % rpw + e * (16 // kb)
+
+
+def scale_pairs_oracle(scale_bits, kb, D):
+    """numpy restatement of the fp16 scale pair table: word t4*D/8 + r of a
+    group = fp16 of the bf16 scales of channels t4*D/4 + dlocal(r, 0/1),
+    low half first."""
+    s = packing.bf16_to_f32(scale_bits.reshape(-1, D)).astype(np.float32)
+    out = np.empty((s.shape[0], D // 2), dtype=np.uint32)
+    for t4 in range(4):
+        for r in range(D // 8):
+            d0, d1 = t4 * D // 4 + _key_dlocal(kb, r, 0), t4 * D // 4 + _key_dlocal(kb, r, 1)
+            lo = s[:, d0].astype(np.float16).view(np.uint16).astype(np.uint32)
+            hi = s[:, d1].astype(np.float16).view(np.uint16).astype(np.uint32)
+            out[:, t4 * D // 8 + r] = lo | (hi << 16)
+    return out
+
+
+@pytest.mark.parametrize("kb,D", [(4, 128), (2, 128), (8, 128), (4, 64), (8, 64)])
+def test_scale_pair_table_layout(kvr, kb, D):
+    """kvr_key_scale_pairs: every word equals the numpy restatement (fp16 of
+    the bf16 scale, channels of the decode's register order), including
+    scales below fp16's normal range."""
+    k, v, q = make((2, 2, 640, D), 12, kb, 4, 32, 0, seed=kb + D)
+    k[0, 0, :, 3] = 0            # constant channel: scale 1e-8/levels, a flushed fp16
+    k[1, 1, :, 5] *= 1e-4        # scales in fp16's subnormal range
+    pk, _ = kvr.pack_kivi_kv(k, v, k_bits=kb, v_bits=4, group_size=32, residual_length=0)
+    got = pk.scale_pairs.contiguous().cpu().numpy().view(np.uint16).reshape(-1, D).view(np.uint32)
+    want = scale_pairs_oracle(bits_of(pk.scale), kb, D)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("kb,vb,D,hq", [(4, 4, 128, 12), (2, 2, 128, 12), (8, 4, 64, 32), (4, 8, 64, 32)])
+def test_scale_pair_table_is_bit_identical(kvr, kb, vb, D, hq):
+    """The decode with the pair table equals the decode converting the bf16
+    scales per chunk, bit for bit (full and ragged chunks, residual window)."""
+    import dataclasses
+
+    k, v, q = make((2, hq // 6 if D == 128 else 8, 3001, D), hq, kb, vb, 32, 128, seed=11 + kb + vb)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=kb, v_bits=vb, group_size=32, residual_length=128)
+    assert pk.scale_pairs is not None
+    bare = dataclasses.replace(pk, scale_pairs=None)
+    for split in (0, 256):
+        a = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=split, out_dtype=F32)
+        b = kvr.packed_kv_decode_attention(q, bare, pv, split_tokens=split, out_dtype=F32)
+        assert torch.equal(a, b), f"split {split}"
+
+
+def test_single_split_full_length(kvr):
+    """The longest accumulation a launch can make: one 32K-token layer in a
+    single split (each warp sums 255 chunks into its tensor-core
+    accumulators), still within the tolerance."""
+    from kv_reduce_b200 import workloads
+
+    wl = workloads.CONFIGS["2"]
+    k, v = workloads.make_layer_kv(wl, 5)
+    q = workloads.make_query(wl, 5)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+    out = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=1 << 20, out_dtype=F32)
+    err = check(out, oracle_out(k, v, q, 4, 4, 32, 128), "32K one split")
+    print(f"one split at 32K: max {err.max():.2e} mean {err.mean():.2e}")

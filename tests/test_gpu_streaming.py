@@ -106,6 +106,10 @@ def test_draft_loop_matches_one_shot(kvr):
     assert cache.prefix_len == kq["P"]
     assert np.array_equal(cache.k.payload.cpu().numpy().reshape(-1), kq["payload"])
     assert np.array_equal(bits_of(cache.k.scale).reshape(-1), kq["scale"].reshape(-1))
+    # the decode's scale pair table, kept through prefill, commits and growth,
+    # equals the table of a one-shot pack
+    one = kvr.key_scale_pairs(cache.k.scale.contiguous(), 4)
+    assert torch.equal(cache.k.scale_pairs, one)
     assert np.array_equal(bits_of(cache.k.residual), kq["residual"])
     assert np.array_equal(cache.v.payload.cpu().numpy().reshape(-1), vq["payload"])
     assert np.array_equal(bits_of(cache.v.scale).reshape(-1), vq["scale"].reshape(-1))
