@@ -693,8 +693,9 @@ def run_ours(args, wl, world, rank, local):
         e2e = {"value": step_bytes * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes, "ms_per_step": e2e_ms,
                "path": "kv_reduce_b200.PackedDecoder.host_step (planned once) each step on the step's stacked "
-                       "pinned host queries: H2D copy, decode of all layers and D2H copy of the outputs replayed "
-                       "as one CUDA graph, then a wait for the outputs"}
+                       "pinned host queries: H2D copy of the queries and the decode of all layers, whose final "
+                       "merge writes the outputs into the pinned host buffer, replayed as one CUDA graph, then a "
+                       "wait for the outputs"}
         e2e_l_ms = time_host(e2e_layers)
         e2e_layers_call = {"value": step_bytes * world / (e2e_l_ms * 1e-3) / 1e9, "unit": "GB/s",
                            "ms_per_step": e2e_l_ms,

@@ -47,6 +47,12 @@ int kvr_version(void);
 const char* kvr_status_string(int status);
 /* Last CUDA error text seen by the library on this host thread ("" if none). */
 const char* kvr_last_error(void);
+/* *mapped = 1 when p points into page-locked host memory that the current
+ * device reads and writes at the same address (unified addressing), so a
+ * kernel may take it as a device pointer, else 0.  No reference
+ * counterpart: the host-buffer decode step uses it to let the decode write
+ * its outputs straight into pinned host memory.                            */
+int kvr_host_mapped(const void* p, int* mapped);
 
 /* ---------------------------------------------------------------- packing
  * Replaces pack_unsigned (packed_kv_cache.py:28-63): n codes (uint8, each

@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "kvr_version",
     "kvr_status_string",
     "kvr_last_error",
+    "kvr_host_mapped",
     "kvr_pack_unsigned",
     "kvr_unpack_unsigned",
     "kvr_quantize_per_token",
@@ -200,6 +201,7 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_attention_lengths.argtypes = [POINTER(DecodeArgs), c_void_p, c_int, c_void_p]
     lib.kvr_decode_step.argtypes = [POINTER(DecodeArgs), c_void_p, c_void_p, c_void_p, c_int, c_void_p]
     lib.kvr_key_scale_pairs.argtypes = [POINTER(ScalePairsArgs), c_void_p]
+    lib.kvr_host_mapped.argtypes = [c_void_p, POINTER(c_int)]
     lib.kvr_exchange_merge.argtypes = [POINTER(ExchangeArgs), c_void_p]
     lib.kvr_exchange_alloc.argtypes = [c_size_t, POINTER(c_void_p), ctypes.c_char_p]
     lib.kvr_exchange_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]
@@ -247,6 +249,14 @@ def call(fn: str, *args) -> None:
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def host_mapped(ptr_value: int) -> bool:
+    """True when a kernel can read and write this pinned host address
+    directly (kvr_host_mapped)."""
+    flag = c_int(0)
+    call("kvr_host_mapped", ptr_value, ctypes.byref(flag))
+    return bool(flag.value)
 
 
 def stream_ptr(device: torch.device) -> int:

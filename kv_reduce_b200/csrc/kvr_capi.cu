@@ -17,6 +17,19 @@ extern "C" int kvr_version(void) { return 100; }  // 0.1.0
 
 extern "C" const char* kvr_last_error(void) { return kvr::g_last_error; }
 
+extern "C" int kvr_host_mapped(const void* p, int* mapped) {
+  if (!mapped) return KVR_ERR_INVALID_ARGUMENT;
+  *mapped = 0;
+  if (!p) return KVR_OK;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    (void)cudaGetLastError();   // memory the runtime does not know: not mapped
+    return KVR_OK;
+  }
+  *mapped = (attr.type == cudaMemoryTypeHost && attr.devicePointer == p) ? 1 : 0;
+  return KVR_OK;
+}
+
 extern "C" const char* kvr_status_string(int status) {
   switch (status) {
     case KVR_OK: return "ok";

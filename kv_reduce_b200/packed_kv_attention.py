@@ -478,58 +478,61 @@ class PackedDecoder:
         are read there (a CPU-side draft controller, a caller that keeps no
         device buffers of its own).  ``queries`` and ``out`` are pinned host
         tensors of the step's shape ([L, B, HQ, 1, D]; bf16 and the decoder's
-        output dtype).  The first call with a pair of buffers copies the
-        queries in, decodes every layer and copies the outputs back once
-        eagerly, then records the same three steps as one CUDA graph on a
-        private stream; every call replays that graph and waits for it, so a
-        step costs one graph launch on the host instead of a copy, a library
-        call per 32 layers and a copy.  Returns ``out`` holding this step's
-        outputs.  The host buffers must stay alive and in place; passing
-        another pair records a new graph.
+        output dtype).  The step copies the queries in (one copy); when the
+        GPU addresses ``out`` directly (pinned memory under unified
+        addressing, kvr_host_mapped) the decode's final merge writes the
+        outputs straight into it, otherwise a copy brings them back.  (Reading
+        the queries the same way measured slower: every split of a (layer,
+        b, kv head) would fetch its query across PCIe.)  The first call with a
+        pair of buffers runs the step eagerly and records it as a CUDA graph
+        on a private stream; every call replays that graph and waits for it.
+        Returns ``out`` holding this step's outputs.  The host buffers must
+        stay alive and in place; passing another pair records a new graph.
         """
+        key = (queries.data_ptr(), out.data_ptr(), tuple(queries.shape), queries.dtype, tuple(out.shape), out.dtype)
+        hs = getattr(self, "_host", None)
+        if hs is not None and hs["key"] == key:
+            hs["graph"].replay()
+            torch.cuda.current_stream(self.device).synchronize()
+            return out
         if (tuple(queries.shape) != self.q_shape or queries.dtype != torch.bfloat16 or queries.is_cuda
                 or not queries.is_pinned() or not queries.is_contiguous()):
             raise ValueError(f"queries must be a contiguous pinned host bf16 tensor of shape {self.q_shape}.")
         if (tuple(out.shape) != self.q_shape or out.dtype != self.out_dtype or out.is_cuda
                 or not out.is_pinned() or not out.is_contiguous()):
             raise ValueError(f"out must be a contiguous pinned host {self.out_dtype} tensor of shape {self.q_shape}.")
-        key = (queries.data_ptr(), out.data_ptr())
-        hs = getattr(self, "_host", None)
-        if hs is None or hs["key"] != key:
-            hs = None
-            self._host = None
-            q_dev = torch.empty(self.q_shape, dtype=torch.bfloat16, device=self.device)
-            o_dev = torch.empty(self.q_shape, dtype=self.out_dtype, device=self.device)
-            stream = torch.cuda.Stream(self.device)
-            layers = []
-            for i, layer in enumerate(self._layers):
-                copy = _lib.LayerPtrs.from_buffer_copy(layer)
-                copy.query = q_dev.data_ptr() + i * self._q_step
-                copy.out = o_dev.data_ptr() + i * self._o_step
-                layers.append(copy)
-            launches = [DecodeLaunch(self.geom, layers[s:s + _lib.KVR_MAX_LAYERS], self.device,
-                                     split_tokens=self.split_tokens, stream=stream.cuda_stream,
-                                     out_fp32=self.out_dtype == torch.float32)
-                        for s in range(0, self.n_layers, _lib.KVR_MAX_LAYERS)]
+        self._host = None
+        zero_copy = _lib.host_mapped(out.data_ptr())   # outputs written in place
+        q_buf = torch.empty(self.q_shape, dtype=torch.bfloat16, device=self.device)
+        o_buf = out if zero_copy else torch.empty(self.q_shape, dtype=self.out_dtype, device=self.device)
+        stream = torch.cuda.Stream(self.device)
+        layers = []
+        for i, layer in enumerate(self._layers):
+            copy = _lib.LayerPtrs.from_buffer_copy(layer)
+            copy.query = q_buf.data_ptr() + i * self._q_step
+            copy.out = o_buf.data_ptr() + i * self._o_step
+            layers.append(copy)
+        launches = [DecodeLaunch(self.geom, layers[s:s + _lib.KVR_MAX_LAYERS], self.device,
+                                 split_tokens=self.split_tokens, stream=stream.cuda_stream,
+                                 out_fp32=self.out_dtype == torch.float32)
+                    for s in range(0, self.n_layers, _lib.KVR_MAX_LAYERS)]
 
-            def step():
-                q_dev.copy_(queries, non_blocking=True)
-                for launch in launches:
-                    launch()
-                out.copy_(o_dev, non_blocking=True)
+        def step():
+            q_buf.copy_(queries, non_blocking=True)
+            for launch in launches:
+                launch()
+            if not zero_copy:
+                out.copy_(o_buf, non_blocking=True)
 
-            stream.wait_stream(torch.cuda.current_stream(self.device))
-            with torch.cuda.stream(stream):
-                step()
-            stream.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                step()
-            self._host = {"key": key, "graph": graph, "buffers": (q_dev, o_dev, queries, out),
-                          "launches": launches, "stream": stream}
-            return out
-        hs["graph"].replay()
-        torch.cuda.current_stream(self.device).synchronize()
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            step()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        self._host = {"key": key, "graph": graph, "buffers": (q_buf, o_buf, queries, out),
+                      "launches": launches, "stream": stream, "zero_copy": zero_copy}
         return out
 
 

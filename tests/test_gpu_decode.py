@@ -298,10 +298,11 @@ def test_packed_decoder_equals_per_layer_calls(kvr):
 @pytest.mark.parametrize("layers,out_dtype", [(3, torch.bfloat16), (35, torch.float32)])
 def test_packed_decoder_host_step(kvr, layers, out_dtype):
     """PackedDecoder.host_step (pinned host queries in, pinned host outputs
-    out; the first call eager, later calls a replayed CUDA graph of copy-in,
-    decode and copy-out) == the device-buffer call, bit for bit, across
-    steps with new query values written into the same host buffer; 35
-    layers take two launches per step."""
+    out; the first call eager, later calls a replayed CUDA graph of the query
+    copy and the decode, whose merge writes the outputs into the pinned
+    buffer directly) == the device-buffer call, bit for bit, across steps
+    with new query values written into the same host buffer; 35 layers take
+    two launches per step."""
     from kv_reduce_b200 import workloads
 
     wl = workloads.CONFIGS["2"].scaled(seq_len=2100, layers=layers)
@@ -319,6 +320,7 @@ def test_packed_decoder_host_step(kvr, layers, out_dtype):
         q_host.copy_(q.cpu())
         assert dec.host_step(q_host, o_host) is o_host
         assert torch.equal(o_host, dec(q).cpu()), f"step {step}"
+    assert dec._host["zero_copy"]   # pinned memory is device-addressable here
     with pytest.raises(ValueError):
         dec.host_step(torch.empty(dec.q_shape, dtype=torch.bfloat16), o_host)
 
