@@ -237,6 +237,16 @@ typedef struct {
 } kvr_scale_pairs_args;
 int kvr_key_scale_pairs(const kvr_scale_pairs_args* a, kvr_stream_t stream);
 
+/* *flag = 1 if a decode on the current device has emitted a non-finite
+ * output since the flag was last cleared (clear != 0 clears it), else 0.
+ * Synchronises the device.  No reference counterpart: the reference
+ * computes in fp32, where this kernel feeds the tensor cores fp16
+ * operands.  Queries are scaled by an exact power of two to |q| < 64;
+ * a key scale, a scaled query times a key scale, or a value scale at or
+ * above 65504 is outside fp16's range, and such a decode's outputs are
+ * non-finite.                                                             */
+int kvr_decode_nonfinite(int* flag, int clear);
+
 /* Fills the split count, workspace bytes and counter count for `a`
  * (workspace and counters ignored). */
 int kvr_decode_plan(const kvr_decode_args* a, int* num_splits,

@@ -23,6 +23,7 @@ from .packed_kv_attention import (  # noqa: F401
     DecodeLaunch,
     PackedDecoder,
     SimtDecodeLaunch,
+    check_finite_outputs,
     lse_merge,
     packed_kv_decode_attention,
     packed_kv_decode_attention_layers,

@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "kvr_decode_attention_lengths",
     "kvr_decode_step",
     "kvr_key_scale_pairs",
+    "kvr_decode_nonfinite",
     "kvr_exchange_merge",
     "kvr_exchange_alloc",
     "kvr_exchange_open",
@@ -202,6 +203,7 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_step.argtypes = [POINTER(DecodeArgs), c_void_p, c_void_p, c_void_p, c_int, c_void_p]
     lib.kvr_key_scale_pairs.argtypes = [POINTER(ScalePairsArgs), c_void_p]
     lib.kvr_host_mapped.argtypes = [c_void_p, POINTER(c_int)]
+    lib.kvr_decode_nonfinite.argtypes = [POINTER(c_int), c_int]
     lib.kvr_exchange_merge.argtypes = [POINTER(ExchangeArgs), c_void_p]
     lib.kvr_exchange_alloc.argtypes = [c_size_t, POINTER(c_void_p), ctypes.c_char_p]
     lib.kvr_exchange_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]

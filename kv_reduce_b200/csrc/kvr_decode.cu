@@ -246,6 +246,15 @@ __device__ __forceinline__ uint32_t key_codes_h2(uint32_t w, int j) {
   const uint32_t x = (j / (8 / B)) ? (w >> 8) : w;
   return x & code_mask<B>(j);
 }
+// Sticky per-device flag: set when a decode emits a non-finite output
+// (an fp16 tensor-core operand out of range: a key scale or q~ = q s / f
+// at or above 65504 after the query scaling below, a value scale at or
+// above 65504), read and cleared by kvr_decode_nonfinite.
+__device__ unsigned int g_decode_nonfinite;
+// Queries with |q| >= 2^kQueryExp are scaled by an exact power of two so
+// |q| < 2^kQueryExp: q / f and q~ = q s / f then stay in fp16 range for key
+// scales below 2^(15 - kQueryExp).  Scores are scaled back in fp32.
+constexpr int kQueryExp = 6;
 constexpr float kKeyUnscale = 16777216.f;          // 2^24
 constexpr float kKeyScale = 1.f / 16777216.f;      // 2^-24
 
@@ -454,8 +463,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
   uint8_t* ring = smem + warp * C::RING;
   const uint32_t ring_s = smem_u32(ring);
   uint4* qs = reinterpret_cast<uint4*>(smem + C::QS_OFF);
-  const float cs = p.score_scale_log2;
-  const float cs_k = cs * kKeyUnscale;   // quantized-key scores carry the codes' 2^-24
+  __shared__ int s_qexp;                 // this item's query exponent shift
 
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
     const int sp = item % NS;
@@ -604,11 +612,31 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     // [D/8, D/4) the raw bf16 pairs of q[dbase .. dbase + D/4).
     if (warp == 0) {
       uint32_t raw[D / 8];
+      float amax = 0.f;
 #pragma unroll
       for (int v = 0; v < D / 32; ++v) {
         uint4 x = head_ok ? __ldg(reinterpret_cast<const uint4*>(qrow + dbase) + v) : make_uint4(0u, 0u, 0u, 0u);
         raw[4 * v + 0] = x.x; raw[4 * v + 1] = x.y; raw[4 * v + 2] = x.z; raw[4 * v + 3] = x.w;
-        qs[(D / 32 + v) * 32 + lane] = x;
+      }
+#pragma unroll
+      for (int w = 0; w < D / 8; ++w) amax = fmaxf(amax, fmaxf(fabsf(bf16lo(raw[w])), fabsf(bf16hi(raw[w]))));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      // |q| >= 2^kQueryExp: scale the query by 2^-qe (exact) so |q| < 2^kQueryExp
+      const int qe = amax >= (float)(1 << kQueryExp) ? min(ilogbf(amax) - kQueryExp + 1, 120) : 0;
+      const float qscale = __int_as_float((127 - qe) << 23);   // 2^-qe, exact
+      if (lane == 0) s_qexp = qe;
+#pragma unroll
+      for (int v = 0; v < D / 32; ++v) {
+        uint32_t wb[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t x = raw[4 * v + k];
+          wb[k] = qe ? ((uint32_t)f32_to_bf16_bits(bf16lo(x) * qscale) |
+                        ((uint32_t)f32_to_bf16_bits(bf16hi(x) * qscale) << 16))
+                     : x;
+        }
+        qs[(D / 32 + v) * 32 + lane] = make_uint4(wb[0], wb[1], wb[2], wb[3]);
       }
 #pragma unroll
       for (int v = 0; v < D / 32; ++v) {
@@ -617,7 +645,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         for (int k = 0; k < 4; ++k) {
           const int r = 4 * v + k;
           const int d0 = key_dlocal<KB>(r, 0), d1 = key_dlocal<KB>(r, 1);
-          const float inv = 1.f / code_factor<KB>(r % C::RPWK);
+          const float inv = qscale / code_factor<KB>(r % C::RPWK);
           const float q0 = ((d0 & 1) ? bf16hi(raw[d0 >> 1]) : bf16lo(raw[d0 >> 1])) * inv;
           const float q1 = ((d1 & 1) ? bf16hi(raw[d1 >> 1]) : bf16lo(raw[d1 >> 1])) * inv;
           w[k] = pack_half2(q0, q1);
@@ -626,6 +654,10 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
       }
     }
     __syncthreads();
+    // score scales of this item: log2(e)/sqrt(D), times the query's 2^qe;
+    // quantized-key scores also carry the codes' 2^-24
+    const float cs = p.score_scale_log2 * __int_as_float((127 + s_qexp) << 23);
+    const float cs_k = cs * kKeyUnscale;
 
     for (int i = 0; i < my_n; ++i) {
       {
@@ -853,6 +885,10 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
         z_run[e] += __shfl_xor_sync(0xffffffffu, z_run[e], o);
       }
     }
+    // NaN scores never raise the running maximum, so the merge would treat
+    // such a warp as empty; its sums still carry the NaN: report it
+    if (!(isfinite(l_run[0]) && isfinite(l_run[1]) && isfinite(z_run[0]) && isfinite(z_run[1])))
+      atomicOr(&g_decode_nonfinite, 1u);
     __syncthreads();   // all warps done with their rings and the query slices
     float* mO = reinterpret_cast<float*>(smem);                 // [W][8][D]
     float* mM = mO + kWarps * kHeads * D;                      // [W][8]
@@ -885,6 +921,8 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     const int64_t pstride = kHeads * (D + 2);
     auto emit = [&](int h, int d, float4 o, float M, float L) {
       const int64_t row = (int64_t)b * p.HQ + kvh * gqa + h;
+      if (!(isfinite(o.x) && isfinite(o.y) && isfinite(o.z) && isfinite(o.w) && isfinite(L)))
+        atomicOr(&g_decode_nonfinite, 1u);   // an fp16 operand left its range
       if (partial_mode) {
         const int64_t prow = (int64_t)layer * p.batch * p.HQ + row;
         *reinterpret_cast<float4*>(p.out_o + prow * D + d) = o;
@@ -1446,6 +1484,23 @@ extern "C" int kvr_key_scale_pairs(const kvr_scale_pairs_args* a, kvr_stream_t s
   KVR_PAIRS(128, 2) KVR_PAIRS(128, 4) KVR_PAIRS(128, 8) KVR_PAIRS(64, 2) KVR_PAIRS(64, 4) KVR_PAIRS(64, 8)
 #undef KVR_PAIRS
   return KVR_ERR_UNSUPPORTED;
+}
+
+extern "C" int kvr_decode_nonfinite(int* flag, int clear) {
+  if (!flag) return KVR_ERR_INVALID_ARGUMENT;
+  cudaError_t e = cudaDeviceSynchronize();
+  unsigned int v = 0;
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, dec::g_decode_nonfinite, sizeof(v));
+  if (e == cudaSuccess && clear && v) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(dec::g_decode_nonfinite, &zero, sizeof(zero));
+  }
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return KVR_ERR_CUDA;
+  }
+  *flag = v ? 1 : 0;
+  return KVR_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -536,6 +536,33 @@ class PackedDecoder:
         return out
 
 
+def check_finite_outputs(device: torch.device | int | None = None, *, clear: bool = True) -> None:
+    """Raise FloatingPointError if a decode on ``device`` has written a
+    non-finite output since the last check (kvr_decode_nonfinite;
+    synchronises the device).
+
+    The reference computes attention in fp32; this kernel feeds the tensor
+    cores fp16 operands.  It scales large queries by an exact power of two
+    (|q| < 64), but a key scale, a scaled query times a key scale, or a
+    value scale at or above 65504 does not fit, and such a decode writes
+    inf/NaN.  Caches whose key or value ranges reach about 1e6 (4-bit codes)
+    are outside the kernel's range: call this after their decodes.
+    """
+    if device is not None:
+        with torch.cuda.device(device):
+            _check_finite(clear)
+    else:
+        _check_finite(clear)
+
+
+def _check_finite(clear: bool) -> None:
+    flag = ctypes.c_int(0)
+    _lib.call("kvr_decode_nonfinite", ctypes.byref(flag), 1 if clear else 0)
+    if flag.value:
+        raise FloatingPointError("a packed-KV decode wrote non-finite outputs: a key scale, query x key scale "
+                                 "or value scale exceeded the fp16 range of the kernel's tensor-core operands")
+
+
 def lse_merge(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Merge per-shard partials: part_ml [n_parts, rows, 2] (m in log2 units, l),
     part_o [n_parts, rows, D] -> bf16 [rows, D]."""

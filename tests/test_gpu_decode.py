@@ -400,3 +400,46 @@ def test_single_split_full_length(kvr):
     out = kvr.packed_kv_decode_attention(q, pk, pv, split_tokens=1 << 20, out_dtype=F32)
     err = check(out, oracle_out(k, v, q, 4, 4, 32, 128), "32K one split")
     print(f"one split at 32K: max {err.max():.2e} mean {err.mean():.2e}")
+
+
+def test_large_query_is_scaled_exactly(kvr):
+    """Queries far beyond fp16's range (|q| ~ 1e5, about 2^17) are scaled by an
+    exact power of two before they meet the tensor cores: the result matches
+    the oracle, and no output is flagged non-finite."""
+    k, v, q = make((1, 2, 1500, 128), 12, 4, 4, 32, 128, seed=41)
+    q = (q.float() * 1e5).to(torch.bfloat16)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+    kvr.check_finite_outputs(clear=True)
+    out = kvr.packed_kv_decode_attention(q, pk, pv, out_dtype=F32)
+    check(out, oracle_out(k, v, q, 4, 4, 32, 128), "|q| ~ 1e5")
+    kvr.check_finite_outputs()
+
+
+def test_outlier_key_channels_x1000(kvr):
+    """Key channels scaled x1000 (group ranges in the thousands): the per-group
+    scales stay inside fp16, the result matches the oracle."""
+    k, v, q = make((1, 2, 2048, 128), 12, 4, 4, 32, 128, seed=43, outliers=0)
+    chans = torch.randperm(128, generator=torch.Generator().manual_seed(43))[:4].cuda()
+    k = k.float()
+    k[..., chans] *= 1000.0
+    k = k.to(torch.bfloat16)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+    out = kvr.packed_kv_decode_attention(q, pk, pv, out_dtype=F32)
+    check(out, oracle_out(k, v, q, 4, 4, 32, 128), "outliers x1000")
+    kvr.check_finite_outputs()
+
+
+def test_key_scale_beyond_fp16_is_flagged(kvr):
+    """A key channel with a range of about 1e7 has a 4-bit scale above fp16's
+    largest value: the decode cannot represent it, and instead of a silent
+    inf/NaN the overflow is reported by check_finite_outputs."""
+    k, v, q = make((1, 2, 1024, 128), 12, 4, 4, 32, 0, seed=47)
+    k = k.float()
+    k[..., 7] *= 3e6
+    k = k.to(torch.bfloat16)
+    pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=0)
+    kvr.check_finite_outputs(clear=True)
+    kvr.packed_kv_decode_attention(q, pk, pv, out_dtype=F32)
+    with pytest.raises(FloatingPointError):
+        kvr.check_finite_outputs()
+    kvr.check_finite_outputs()   # the check cleared the flag
