@@ -70,8 +70,11 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--nccl-exchange", action="store_true",
-                   help="--split-sequence: exchange partials with NCCL all-gather instead of the fused kernel")
+    p.add_argument("--exchange", choices=["delivered", "push", "nccl"], default="delivered",
+                   help="sequence split's exchange: the decode stores its rows into the peers and one kernel "
+                        "waits and merges (delivered), one kernel pushes, signals and merges (push), or an "
+                        "NCCL all-gather plus the LSE merge launch (nccl)")
+    p.add_argument("--nccl-exchange", action="store_true", help="same as --exchange nccl")
     p.add_argument("--draft-loop", action="store_true",
                    help="speculative draft loop on the streaming cache (use with --config 5)")
     p.add_argument("--split-sequence", action="store_true",
@@ -474,16 +477,20 @@ def measure_draft_loop(args, world, rank, device, pg_sync):
     return res
 
 
-def measure_split_sequence(args, wl, world, rank, device, nccl_exchange=False):
+def measure_split_sequence(args, wl, world, rank, device, mode="delivered"):
     """One batch-1 sequence, its tokens split across the ranks (strong scaling).
 
     Each rank packs every layer and keeps its 32-token-aligned token shard
     (kv_reduce_b200.distributed.shard_component); a step is one partial
-    decode launch over all layers of the shard and one exchange kernel that
-    stores the (m, l, o) partials into every peer over NVLink and merges
-    them (nccl_exchange: an NCCL all-gather and the LSE merge kernel).  The
-    step time is the max over ranks; the result counts the whole sequence's
-    bytes once.  Returns the sub-dict (rank 0) and the exchange error count.
+    decode launch over all layers of the shard and one exchange kernel.
+    mode "delivered": the decode stores each finished row of (m, l, o)
+    partials into every peer over NVLink and releases a per-row flag; the
+    exchange kernel waits for the flags and merges.  "push": the decode
+    writes its partials locally; the exchange kernel stores them into every
+    peer, signals and merges.  "nccl": an NCCL all-gather and the LSE merge
+    kernel.  The step time is the max over ranks; the result counts the
+    whole sequence's bytes once.  Returns the sub-dict (rank 0) and the
+    exchange error count.
     """
     import torch.distributed as dist
 
@@ -510,12 +517,16 @@ def measure_split_sequence(args, wl, world, rank, device, nccl_exchange=False):
     launch = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
                           split_tokens=args.split_tokens)
     out = torch.empty(rows, wl.head_dim, dtype=torch.bfloat16, device=device)
-    p2p = world > 1 and not nccl_exchange
+    p2p = world > 1 and mode != "nccl"
+    delivered = mode == "delivered"
     if p2p:
         xchg = kd.PeerExchange(rows, wl.head_dim, device)
 
         def step():
-            xchg.step(launch.partial)
+            if delivered:
+                xchg.step_delivered(launch)
+            else:
+                xchg.step(launch.partial)
     else:
         dec = kd.SequenceShardDecoder(rows, wl.head_dim, world, device, partial_fn=launch.partial,
                                       merge_fn=lambda ml, o: kvr.lse_merge(ml, o, out=out))
@@ -533,7 +544,7 @@ def measure_split_sequence(args, wl, world, rank, device, nccl_exchange=False):
         side = torch.cuda.Stream(device)
         launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
                                 split_tokens=args.split_tokens, stream=side.cuda_stream)
-        graph = xchg.capture_pair(launch_g.partial, side)
+        graph = xchg.capture_pair(launch_g if delivered else launch_g.partial, side, delivered=delivered)
         for _ in range(2):
             xchg.replay_pair(graph)
         torch.cuda.synchronize()
@@ -563,7 +574,9 @@ def measure_split_sequence(args, wl, world, rank, device, nccl_exchange=False):
            "parallelism": f"token-split x{world}", "shard_tokens": b - a, "num_splits": launch.num_splits,
            "us_per_step": ms * 1e3, "gbps": value, "tokens_per_s": wl.batch / (ms * 1e-3),
            "frac_per_gpu": value / world / peak, "frac_note": "of measured, per GPU", "steps": n_steps,
-           "exchange": ("one kernel: NVLink peer stores + signal + LSE merge" if p2p else
+           "exchange": ("decode stores rows into the peers over NVLink + per-row flags; one wait-and-merge kernel"
+                        if p2p and delivered else
+                        "one kernel: NVLink peer stores + signal + LSE merge" if p2p else
                         "NCCL all-gather + LSE merge launch" if world > 1 else "none"),
            "exchange_errors": errors, "scaling": "strong (one sequence)",
            "timing": ("CUDA graph of two steps (partial decode of all layers + fused exchange)"
@@ -728,7 +741,7 @@ def run_ours(args, wl, world, rank, local):
     split_errors = 0
     if world > 1 and not args.no_workloads:
         pg_sync()
-        split, split_errors = measure_split_sequence(args, wl, world, rank, device)
+        split, split_errors = measure_split_sequence(args, wl, world, rank, device, mode=exchange_mode(args))
 
     if rank == 0:
         config = workload_config(wl, world, args)
@@ -764,12 +777,16 @@ def run_ours(args, wl, world, rank, local):
         raise SystemExit(f"{split_errors} exchange wait(s) timed out in the sequence split")
 
 
+def exchange_mode(args) -> str:
+    return "nccl" if args.nccl_exchange else args.exchange
+
+
 def run_split_sequence(args, wl, world, rank, local):
     """--split-sequence: the sequence split as the whole line."""
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     init_pg(world, device)
-    res, errors = measure_split_sequence(args, wl, world, rank, device, nccl_exchange=args.nccl_exchange)
+    res, errors = measure_split_sequence(args, wl, world, rank, device, mode=exchange_mode(args))
     if rank == 0:
         line = {"metric": METRIC, "value": res["gbps"], "unit": "GB/s", "n_gpus": world, "steps": res["steps"],
                 "warmup": args.warmup, "ms_per_step": res["us_per_step"] / 1e3, "us_per_step": res["us_per_step"],

@@ -342,6 +342,24 @@ typedef struct {
 } kvr_exchange_args;
 int kvr_exchange_merge(const kvr_exchange_args* a, kvr_stream_t stream);
 
+/* Delivered mode (head_dim 64 or 128, world <= 8): kvr_decode_partial_exchange
+ * runs the decode over [token_begin, token_end) and, instead of writing
+ * partials locally, stores each finished row straight into this rank's
+ * slot of every rank's receive area as 8-byte words (value bits, epoch),
+ * each written whole (the low-latency protocol NCCL publishes as "LL"):
+ * uint32 words [2 halves][world sources][rows][2 + D][2] at byte offset
+ * 256 of each signal area, row = (m, l, o[0..D)), half = step % 2.  No
+ * fence and no flag: kvr_exchange_merge_delivered reads every source's
+ * words for a row until all carry this step's epoch (bounded by
+ * timeout_ns; a time-out sets *error), merges the row from local memory
+ * and advances the epoch.  The buffer of each rank is then
+ * 8*world*rows*(2+D) + 256 + 16*world*rows*(2+D) bytes.  x->rows must be
+ * n_layers*batch*q_heads; recv, out, counter and timeout_ns are not used
+ * by the decode.                                                           */
+int kvr_decode_partial_exchange(const kvr_decode_args* a, int token_begin, int token_end,
+                                const kvr_exchange_args* x, kvr_stream_t stream);
+int kvr_exchange_merge_delivered(const kvr_exchange_args* a, kvr_stream_t stream);
+
 /* Receive buffers shared between processes: device memory from cudaMalloc
  * (zeroed) with a 64-byte CUDA IPC handle; a peer maps it with
  * kvr_exchange_open and unmaps it with kvr_exchange_close.                 */

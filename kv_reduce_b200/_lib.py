@@ -54,6 +54,8 @@ EXPORTED_SYMBOLS = (
     "kvr_key_scale_pairs",
     "kvr_decode_nonfinite",
     "kvr_exchange_merge",
+    "kvr_exchange_merge_delivered",
+    "kvr_decode_partial_exchange",
     "kvr_exchange_alloc",
     "kvr_exchange_open",
     "kvr_exchange_close",
@@ -205,6 +207,8 @@ def load() -> ctypes.CDLL:
     lib.kvr_host_mapped.argtypes = [c_void_p, POINTER(c_int)]
     lib.kvr_decode_nonfinite.argtypes = [POINTER(c_int), c_int]
     lib.kvr_exchange_merge.argtypes = [POINTER(ExchangeArgs), c_void_p]
+    lib.kvr_exchange_merge_delivered.argtypes = [POINTER(ExchangeArgs), c_void_p]
+    lib.kvr_decode_partial_exchange.argtypes = [POINTER(DecodeArgs), c_int, c_int, POINTER(ExchangeArgs), c_void_p]
     lib.kvr_exchange_alloc.argtypes = [c_size_t, POINTER(c_void_p), ctypes.c_char_p]
     lib.kvr_exchange_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]
     lib.kvr_exchange_close.argtypes = [c_void_p]

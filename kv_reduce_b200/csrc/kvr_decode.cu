@@ -134,7 +134,14 @@ struct Params {
   // value row is quantized per token, and the sequence length advances
   const uint16_t* app_k;         // [B, HKV, 1, D] bf16, or null
   const uint16_t* app_v;
+  // fused sequence-split exchange (partial mode, kvr_decode_partial_exchange):
+  // the partials of this launch go, as (value, epoch) words, to half
+  // (epoch % 2), source slot x_rank, of every rank's receive area
+  int* const* x_signal;          // device array [x_world]: signal areas (receive areas at +kLLWords), or null
+  const int* x_epoch;            // exchanges completed on this rank; this step is *x_epoch + 1
+  int x_world, x_rank;
 };
+constexpr int kLLWords = 64;     // 32-bit words of a signal area before its receive area
 
 // Append one token of unit bh (one warp; lane = D/32 channels): the key row
 // into the BF16 residual at res_row, the value row quantized per token into
@@ -201,6 +208,13 @@ __device__ __forceinline__ float4 dsmem_f32x4(uint32_t addr) {
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
   return v;
+}
+
+// one 16-byte store of two (value, tag) words; volatile, so it is issued
+// as written and each 8-byte half lands whole
+__device__ __forceinline__ void st_volatile_v4(uint32_t* ptr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"l"(ptr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
 }
 
 // ----------------------------------------------------------- register maps
@@ -416,11 +430,14 @@ __device__ __forceinline__ void qk_prefix(float (&hi)[4], float (&lo)[4], const 
   }
 }
 
-template <int D, int KB, int VB, int MAXL>
+// XCHG: the fused-exchange instantiation (kvr_decode_partial_exchange); the
+// others compile its stores and flag releases out
+template <int D, int KB, int VB, int MAXL, bool XCHG = false>
 __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_kernel(const __grid_constant__ Params<MAXL> p) {
   using C = Cfg<D, KB, VB>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_flag;
+  __shared__ int s_xe;   // fused exchange: this step's epoch
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int g = lane >> 2, t4 = lane & 3;
@@ -429,6 +446,9 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
   const int NS = p.num_splits;
   const int log2G = p.log2G;
   pdl_wait();   // nothing above touches global memory
+  // the exchange of the previous step completed before pdl_wait returned,
+  // so its epoch update is visible; read once, used after the CTA barriers
+  if (XCHG && threadIdx.x == 0) s_xe = p.x_signal ? *reinterpret_cast<const volatile int*>(p.x_epoch) + 1 : 0;
   // Lengths: from the launch, or (graph-replayable loops) from device memory,
   // clamped to the capacities the host validated: sequence <= tok_end,
   // prefix <= P in whole groups, residual rows <= res_cap.
@@ -917,16 +937,35 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
 
     // ------------------------------------------------- CTA merge of the warps
     const int gqa = p.gqa;
-    const bool partial_mode = p.out_ml != nullptr;
+    const bool xchg_mode = XCHG && p.x_signal != nullptr;
+    const bool partial_mode = p.out_ml != nullptr || xchg_mode;
+    const int64_t x_rows = (int64_t)p.n_layers * p.batch * p.HQ;
     const int64_t pstride = kHeads * (D + 2);
+    const int x_e = xchg_mode ? s_xe : 0;
     auto emit = [&](int h, int d, float4 o, float M, float L) {
       const int64_t row = (int64_t)b * p.HQ + kvh * gqa + h;
       if (!(isfinite(o.x) && isfinite(o.y) && isfinite(o.z) && isfinite(o.w) && isfinite(L)))
         atomicOr(&g_decode_nonfinite, 1u);   // an fp16 operand left its range
       if (partial_mode) {
         const int64_t prow = (int64_t)layer * p.batch * p.HQ + row;
-        *reinterpret_cast<float4*>(p.out_o + prow * D + d) = o;
-        if (d == 0) { p.out_ml[2 * prow] = M; p.out_ml[2 * prow + 1] = L; }
+        if (xchg_mode) {
+          // every rank's receive area, this rank's slot of the step's half:
+          // each 8-byte word is (value, epoch), written whole, so the
+          // receiver validates every word by its tag and nothing here waits
+          // for the stores to land (no fence, no flag)
+          const uint32_t e = (uint32_t)x_e;
+          const int64_t lslot = x_rows * (2 + D) * 2;   // 32-bit words per (half, source)
+          for (int r = 0; r < p.x_world; ++r) {
+            uint32_t* base = reinterpret_cast<uint32_t*>(p.x_signal[r]) + kLLWords +
+                             ((int64_t)(x_e & 1) * p.x_world + p.x_rank) * lslot + prow * (2 + D) * 2;
+            st_volatile_v4(base + 2 * (2 + d), __float_as_uint(o.x), e, __float_as_uint(o.y), e);
+            st_volatile_v4(base + 2 * (2 + d + 2), __float_as_uint(o.z), e, __float_as_uint(o.w), e);
+            if (d == 0) st_volatile_v4(base, __float_as_uint(M), e, __float_as_uint(L), e);
+          }
+        } else {
+          *reinterpret_cast<float4*>(p.out_o + prow * D + d) = o;
+          if (d == 0) { p.out_ml[2 * prow] = M; p.out_ml[2 * prow + 1] = L; }
+        }
       } else {
         const float inv = L > 0.f ? 1.f / L : 0.f;
         const float4 r = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
@@ -1015,12 +1054,13 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
           L = fmaf(wt, ls[s], L);
         }
         if (M == NEG_INF) { o = make_float4(0.f, 0.f, 0.f, 0.f); L = 0.f; }
-        if (!dl) continue;
-        if (dst) {
-          *reinterpret_cast<float4*>(dst + 2 * kHeads + h * D + d) = o;
-          if (d == 0) { dst[h] = M; dst[kHeads + h] = L; }
-        } else {
-          emit(h, d, o, M, L);
+        if (dl) {
+          if (dst) {
+            *reinterpret_cast<float4*>(dst + 2 * kHeads + h * D + d) = o;
+            if (d == 0) { dst[h] = M; dst[kHeads + h] = L; }
+          } else {
+            emit(h, d, o, M, L);
+          }
         }
       }
     };
@@ -1253,14 +1293,18 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   p.cluster = pl.cluster;
   p.app_k = nullptr;
   p.app_v = nullptr;
+  p.x_signal = nullptr;
+  p.x_epoch = nullptr;
+  p.x_world = 0;
+  p.x_rank = 0;
 }
 
 // Per-device, per-instantiation set-up: dynamic shared memory limit and
 // resident CTAs per SM (a benign race sets the same values).
-template <int D, int KB, int VB, int MAXL>
+template <int D, int KB, int VB, int MAXL, bool XCHG = false>
 static int prepare(int* ctas_per_sm) {
   using C = Cfg<D, KB, VB>;
-  auto kern = decode_kernel<D, KB, VB, MAXL>;
+  auto kern = decode_kernel<D, KB, VB, MAXL, XCHG>;
   static int occ[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
@@ -1286,7 +1330,7 @@ static int prepare(int* ctas_per_sm) {
 
 // Clusters of `cl` CTAs that can be resident at once on this device (0 when
 // the size is unsupported), per device and size.
-template <int D, int KB, int VB, int MAXL>
+template <int D, int KB, int VB, int MAXL, bool XCHG = false>
 static int active_clusters(int cl) {
   static int cache[64][17];
   static bool init[64][17];
@@ -1307,7 +1351,7 @@ static int active_clusters(int cl) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel<D, KB, VB, MAXL>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel<D, KB, VB, MAXL, XCHG>, &cfg) != cudaSuccess) {
       (void)cudaGetLastError();
       n = 0;
     }
@@ -1324,27 +1368,39 @@ static int active_clusters(int cl) {
 // With more splits, clusters of kFan plus a global level measured slower on
 // B200 than two global levels (uneven cluster placement over the GPCs and a
 // costlier launch), so those plans keep the global merge.
-template <int D, int KB, int VB, int MAXL>
+template <int D, int KB, int VB, int MAXL, bool XCHG = false>
 static int cluster_for(const Plan& pl) {
   const int ns = pl.num_splits;
   if (ns < 2 || ns > kFan || pl.items > pl.grid) return 1;
-  const int n = active_clusters<D, KB, VB, MAXL>(ns);
+  const int n = active_clusters<D, KB, VB, MAXL, XCHG>(ns);
   return (n > 0 && pl.items / ns <= n) ? ns : 1;
 }
 
-template <int D, int KB, int VB, int MAXL>
+template <int D, int KB, int VB, int MAXL, bool XCHG = false>
 static void launch(const Params<MAXL>& p, const Plan& pl, cudaStream_t s) {
-  (void)pdl_launch(decode_kernel<D, KB, VB, MAXL>, dim3(pl.grid), dim3(kWarps * 32), Cfg<D, KB, VB>::SMEM, s,
+  (void)pdl_launch(decode_kernel<D, KB, VB, MAXL, XCHG>, dim3(pl.grid), dim3(kWarps * 32), Cfg<D, KB, VB>::SMEM, s,
                    pl.cluster, p);
+}
+
+template <int MAXL>
+static void set_exchange(Params<MAXL>& p, const kvr_exchange_args* x) {
+  if (!x) return;
+  p.x_signal = x->signal;
+  p.x_epoch = x->epoch;
+  p.x_world = x->world;
+  p.x_rank = x->rank;
 }
 
 template <int D, int KB, int VB>
 static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float* out_o, cudaStream_t s,
                  Plan* plan_only, const int* dev_len, int res_cap, const uint16_t* app_k,
-                 const uint16_t* app_v) {
+                 const uint16_t* app_v, const kvr_exchange_args* x) {
   using C = Cfg<D, KB, VB>;
   int occ = 3;
-  const int dev_st = (a->n_layers == 1) ? prepare<D, KB, VB, 1>(&occ) : prepare<D, KB, VB, KVR_MAX_LAYERS>(&occ);
+  // the fused exchange has one instantiation, over the multi-layer parameter block
+  const int dev_st = x                     ? prepare<D, KB, VB, KVR_MAX_LAYERS, true>(&occ)
+                     : (a->n_layers == 1) ? prepare<D, KB, VB, 1>(&occ)
+                                          : prepare<D, KB, VB, KVR_MAX_LAYERS>(&occ);
   if (dev_st != KVR_OK) {
     // no usable device: plan with a shared-memory-bound estimate; argument
     // errors below still take precedence over the device error
@@ -1357,7 +1413,7 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
     if (!aligned16(a->workspace)) return KVR_ERR_MISALIGNED;
   }
   if (dev_st != KVR_OK) return dev_st;
-  if (a->n_layers == 1) {
+  if (a->n_layers == 1 && !x) {
     pl.cluster = cluster_for<D, KB, VB, 1>(pl);
     Params<1> p;
     fill_params(p, a, pl, tb, te);
@@ -1365,6 +1421,12 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
     if (dev_len) { p.dev_len = const_cast<int*>(dev_len); p.res_cap = res_cap; }
     p.app_k = app_k; p.app_v = app_v;
     launch<D, KB, VB, 1>(p, pl, s);
+  } else if (x) {
+    pl.cluster = cluster_for<D, KB, VB, KVR_MAX_LAYERS, true>(pl);
+    Params<KVR_MAX_LAYERS> p;
+    fill_params(p, a, pl, tb, te);
+    set_exchange(p, x);
+    launch<D, KB, VB, KVR_MAX_LAYERS, true>(p, pl, s);
   } else {
     pl.cluster = cluster_for<D, KB, VB, KVR_MAX_LAYERS>(pl);
     Params<KVR_MAX_LAYERS> p;
@@ -1379,13 +1441,14 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
 
 static int run(const kvr_decode_args* a, int tb, int te, float* out_ml, float* out_o, cudaStream_t s,
                Plan* plan_only = nullptr, const int* dev_len = nullptr, int res_cap = 0,
-               const uint16_t* app_k = nullptr, const uint16_t* app_v = nullptr) {
+               const uint16_t* app_k = nullptr, const uint16_t* app_v = nullptr,
+               const kvr_exchange_args* x = nullptr) {
   int st = validate(a);
   if (st != KVR_OK) return st;
   if (tb < 0 || te > a->seq_len || tb >= te || tb % kChunk) return KVR_ERR_INVALID_ARGUMENT;
 #define KVR_CASE(D_, KB_, VB_)                                                              \
   if (a->head_dim == D_ && a->key_bits == KB_ && a->value_bits == VB_)                      \
-    return run_t<D_, KB_, VB_>(a, tb, te, out_ml, out_o, s, plan_only, dev_len, res_cap, app_k, app_v);
+    return run_t<D_, KB_, VB_>(a, tb, te, out_ml, out_o, s, plan_only, dev_len, res_cap, app_k, app_v, x);
   KVR_CASE(128, 4, 4) KVR_CASE(128, 8, 4) KVR_CASE(128, 4, 8) KVR_CASE(128, 8, 8)
   KVR_CASE(128, 2, 2) KVR_CASE(128, 2, 4) KVR_CASE(128, 4, 2) KVR_CASE(128, 8, 2) KVR_CASE(128, 2, 8)
   KVR_CASE(64, 4, 4) KVR_CASE(64, 8, 4) KVR_CASE(64, 4, 8) KVR_CASE(64, 8, 8) KVR_CASE(64, 2, 4)
@@ -1437,6 +1500,15 @@ extern "C" int kvr_decode_partial(const kvr_decode_args* a, int token_begin, int
                                   float* part_o, kvr_stream_t stream) {
   if (!a || !part_ml || !part_o) return KVR_ERR_INVALID_ARGUMENT;
   return dec::run(a, token_begin, token_end, part_ml, part_o, as_stream(stream));
+}
+
+extern "C" int kvr_decode_partial_exchange(const kvr_decode_args* a, int token_begin, int token_end,
+                                           const kvr_exchange_args* x, kvr_stream_t stream) {
+  if (!a || !x || x->world < 1 || x->world > 8 || x->rank < 0 || x->rank >= x->world || !x->signal || !x->epoch)
+    return KVR_ERR_INVALID_ARGUMENT;
+  if (x->rows != a->n_layers * a->batch * a->q_heads || x->head_dim != a->head_dim) return KVR_ERR_INVALID_ARGUMENT;
+  return dec::run(a, token_begin, token_end, nullptr, nullptr, as_stream(stream), nullptr, nullptr, 0, nullptr,
+                  nullptr, x);
 }
 
 // ---------------------------------------------------------------------------

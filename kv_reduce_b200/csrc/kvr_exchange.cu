@@ -128,6 +128,97 @@ __global__ void __launch_bounds__(kThreads) exchange_merge_kernel(kvr_exchange_a
   }
 }
 
+// Delivered mode: kvr_decode_partial_exchange has already stored every row
+// of this step's partials into each rank's receive area as 8-byte words
+// (value, epoch), each written whole -- the low-latency protocol NCCL
+// publishes as "LL".  Nothing is pushed or fenced here: one warp per row
+// reads every source's words for the row until all of them carry this
+// step's epoch (bounded by the launch's deadline), then merges the row.
+// The last CTA to finish advances the epoch.
+constexpr int kLLWords = 64;   // receive area: 32-bit words after the signal words
+
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kThreads) merge_delivered_kernel(kvr_exchange_args a) {
+  // launched as a programmatic dependent of this rank's decode: resident
+  // early, but nothing is read before that decode has completed
+  pdl_wait();
+  const int world = a.world, rank = a.rank, rows = a.rows, D = a.head_dim;
+  const int ep = *reinterpret_cast<volatile int*>(a.epoch) + 1;
+  const uint32_t e = (uint32_t)ep;
+  const int64_t lslot = (int64_t)rows * (2 + D) * 2;   // words per (half, source)
+  const uint32_t* area = reinterpret_cast<const uint32_t*>(a.signal[rank]) + kLLWords + (int64_t)(ep & 1) * world * lslot;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const int d = 4 * lane;
+  const bool dl = d < D;
+  const uint64_t deadline = global_timer_ns() + (uint64_t)a.timeout_ns;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  bool timed_out = false;
+  for (int row = blockIdx.x * warps + warp; row < rows; row += gridDim.x * warps) {
+    // every source's (m, l) words and this lane's four o words, all loads
+    // in flight at once; then only the words whose tag is not yet this
+    // step's are read again, until the deadline
+    uint4 wml[8], wo0[8], wo1[8];
+    const uint4 zero = make_uint4(0u, e, 0u, e);
+#pragma unroll
+    for (int src = 0; src < 8; ++src) {
+      const uint32_t* r = area + src * lslot + (int64_t)row * (2 + D) * 2;
+      wml[src] = src < world ? ld_volatile_v4(r) : zero;
+      wo0[src] = (src < world && dl) ? ld_volatile_v4(r + 2 * (2 + d)) : zero;
+      wo1[src] = (src < world && dl) ? ld_volatile_v4(r + 2 * (2 + d) + 4) : zero;
+    }
+    for (;;) {
+      bool ready = true;
+#pragma unroll
+      for (int src = 0; src < 8; ++src) {
+        if (src >= world) break;
+        const uint32_t* r = area + src * lslot + (int64_t)row * (2 + D) * 2;
+        if (wml[src].y != e || wml[src].w != e) { ready = false; wml[src] = ld_volatile_v4(r); }
+        if (wo0[src].y != e || wo0[src].w != e) { ready = false; wo0[src] = ld_volatile_v4(r + 2 * (2 + d)); }
+        if (wo1[src].y != e || wo1[src].w != e) { ready = false; wo1[src] = ld_volatile_v4(r + 2 * (2 + d) + 4); }
+      }
+      if (ready || timed_out) break;
+      if (global_timer_ns() > deadline) timed_out = true;   // one more pass, then merge what is there
+    }
+    float M = NEG_INF;
+#pragma unroll
+    for (int src = 0; src < 8; ++src)
+      if (src < world) M = fmaxf(M, __uint_as_float(wml[src].x));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+#pragma unroll
+    for (int src = 0; src < 8; ++src) {
+      if (src >= world) break;
+      const float m = __uint_as_float(wml[src].x);
+      if (M == NEG_INF || m == NEG_INF) continue;
+      const float wt = exp2f(m - M);
+      acc.x = fmaf(wt, __uint_as_float(wo0[src].x), acc.x); acc.y = fmaf(wt, __uint_as_float(wo0[src].z), acc.y);
+      acc.z = fmaf(wt, __uint_as_float(wo1[src].x), acc.z); acc.w = fmaf(wt, __uint_as_float(wo1[src].z), acc.w);
+      L = fmaf(wt, __uint_as_float(wml[src].z), L);
+    }
+    if (dl) {
+      // acc / L as in kvr_lse_merge, so the two merges agree bit for bit
+      const bool nz = L > 0.f;
+      uint2 pk;
+      pk.x = (uint32_t)f32_to_bf16_bits(nz ? acc.x / L : 0.f) | ((uint32_t)f32_to_bf16_bits(nz ? acc.y / L : 0.f) << 16);
+      pk.y = (uint32_t)f32_to_bf16_bits(nz ? acc.z / L : 0.f) | ((uint32_t)f32_to_bf16_bits(nz ? acc.w / L : 0.f) << 16);
+      *reinterpret_cast<uint2*>(a.out + (int64_t)row * D + d) = pk;
+    }
+  }
+  if (timed_out) atomicOr(a.error, 1);   // some row merged whatever was there: the output is invalid
+  // every CTA has read the epoch before it arrives; the last one advances it
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(a.counter, 1) == (int)gridDim.x - 1) {
+    *a.counter = 0;
+    *a.epoch = ep;
+  }
+}
+
 }  // namespace xchg
 }  // namespace kvr
 
@@ -184,5 +275,19 @@ extern "C" int kvr_exchange_merge(const kvr_exchange_args* a, kvr_stream_t strea
   const int64_t work = (int64_t)a->rows * (2 + a->head_dim);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, (work + xchg::kThreads - 1) / xchg::kThreads));
   xchg::exchange_merge_kernel<<<grid, xchg::kThreads, 0, as_stream(stream)>>>(*a);
+  return check_launch();
+}
+
+extern "C" int kvr_exchange_merge_delivered(const kvr_exchange_args* a, kvr_stream_t stream) {
+  if (!a || a->world < 1 || a->world > 8 || a->rank < 0 || a->rank >= a->world || a->rows < 1 ||
+      (a->head_dim != 64 && a->head_dim != 128) || !a->signal || !a->epoch || !a->counter || !a->out ||
+      !a->error || a->timeout_ns <= 0)
+    return KVR_ERR_INVALID_ARGUMENT;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // one warp per row, one CTA per SM at most: every CTA is resident while it waits
+  constexpr int warps = xchg::kThreads / 32;
+  const int grid = std::max(1, std::min(sms, (a->rows + warps - 1) / warps));
+  (void)pdl_launch(xchg::merge_delivered_kernel, dim3(grid), dim3(xchg::kThreads), 0, as_stream(stream), 1, *a);
   return check_launch();
 }

@@ -71,13 +71,16 @@ def shard_component(k: PackedKVComponent, v: PackedKVComponent, begin: int, end:
     kp = k.payload.reshape(B, H, P, rbk)[:, :, begin:begin + n_pref].contiguous().reshape(-1)
     ks = k.scale.reshape(B, H, P // G, 1, D)[:, :, begin // G:(begin + n_pref) // G].contiguous()
     ko = k.offset.reshape(B, H, P // G, 1, D)[:, :, begin // G:(begin + n_pref) // G].contiguous()
+    # the decode's fp16 scale pairs are per group: the shard keeps its groups' rows
+    ksp = (k.scale_pairs.reshape(B, H, P // G, 1, D)[:, :, begin // G:(begin + n_pref) // G].contiguous()
+           if k.scale_pairs is not None else None)
     r0, r1 = max(begin, P) - P, max(end, P) - P
     res = k.residual[:, :, r0:r1].contiguous() if k.residual is not None else None
     vp = v.payload.reshape(B, H, S, rbv)[:, :, begin:end].contiguous().reshape(-1)
     vs = v.scale.reshape(B, H, S, 1)[:, :, begin:end].contiguous()
     vo = v.offset.reshape(B, H, S, 1)[:, :, begin:end].contiguous()
     shape = (B, H, end - begin, D)
-    ks_out = PackedKVComponent(kp, ks, ko, res, shape, kb, k.layout, k.output_dtype, G, n_pref)
+    ks_out = PackedKVComponent(kp, ks, ko, res, shape, kb, k.layout, k.output_dtype, G, n_pref, scale_pairs=ksp)
     vs_out = PackedKVComponent(vp, vs, vo, None, shape, vb, v.layout, v.output_dtype)
     return ks_out, vs_out
 
@@ -160,6 +163,14 @@ class PeerExchange:
     ``timeout_s``) and merges all ranks into the bf16 output -- one kernel in
     place of an all-gather collective and a merge launch.  All ranks make the
     same calls in the same order; ``close()`` is collective too.
+
+    ``step_delivered(launch)`` is the fused form for a DecodeLaunch over this
+    rank's token shard: the decode kernel itself stores every finished row
+    of partials into each rank's receive area as (value, epoch) words
+    (kvr_decode_partial_exchange), so the rows cross NVLink while the
+    decode is still running and nothing is fenced; the exchange kernel
+    (kvr_exchange_merge_delivered) reads the words until every one carries
+    the step's epoch, and merges.
     """
 
     def __init__(self, rows: int, head_dim: int, device: torch.device, group=None,
@@ -175,9 +186,10 @@ class PeerExchange:
         self.rows, self.head_dim, self.device, self.group = int(rows), int(head_dim), device, group
         slot = self.rows * (2 + self.head_dim)
         data_bytes = 2 * self.world * slot * 4
+        ll_bytes = 2 * data_bytes   # delivered mode: (value, epoch) words after the signal area
         own = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
-        _lib.call("kvr_exchange_alloc", data_bytes + 256, ctypes.byref(own), handle)
+        _lib.call("kvr_exchange_alloc", data_bytes + 256 + ll_bytes, ctypes.byref(own), handle)
         self._own = own.value
         mine = torch.tensor(list(handle.raw), dtype=torch.uint8, device=device)
         handles = torch.empty(self.world, 64, dtype=torch.uint8, device=device)
@@ -223,20 +235,42 @@ class PeerExchange:
         self.steps = n
         return self.out
 
+    def step_delivered(self, launch) -> torch.Tensor:
+        """One step of the delivered mode on ``launch``'s stream: the decode
+        over launch's token range with its rows stored into every rank's
+        receive buffer, then the wait-and-merge kernel."""
+        import ctypes
+
+        from . import _lib
+
+        if launch.geom.head_dim != self.head_dim or len(launch.layers) * launch.geom.batch * launch.geom.q_heads != self.rows:
+            raise ValueError("the launch's rows (layers x batch x q_heads) and head_dim must match the exchange")
+        lib = _lib.load()
+        _lib.check("kvr_decode_partial_exchange", lib.kvr_decode_partial_exchange(
+            launch.args, launch.token_begin, launch.token_end, ctypes.byref(self._args), launch.stream))
+        _lib.check("kvr_exchange_merge_delivered", lib.kvr_exchange_merge_delivered(self._args, launch.stream))
+        self.steps += 1
+        return self.out
+
     def capture_pair(self, partial_fn: Callable[[torch.Tensor, torch.Tensor], None],
-                     stream: torch.cuda.Stream) -> torch.cuda.CUDAGraph:
+                     stream: torch.cuda.Stream, delivered: bool = False) -> torch.cuda.CUDAGraph:
         """Record two consecutive steps -- one per receive half -- into a CUDA
-        graph on `stream` (partial_fn must launch on the current stream).  The
-        exchange kernel reads its epoch from device memory, so the graph can
-        be replayed any number of times with ``replay_pair``; every rank
-        records and replays its pair in step with the others."""
+        graph on `stream` (partial_fn must launch on the current stream; with
+        ``delivered``, partial_fn is a DecodeLaunch bound to `stream` and the
+        steps are ``step_delivered``).  The exchange kernels read their epoch
+        from device memory, so the graph can be replayed any number of times
+        with ``replay_pair``; every rank records and replays its pair in step
+        with the others."""
         if self.steps % 2:
             raise ValueError("capture after an even number of steps")
         g = torch.cuda.CUDAGraph()
         torch.cuda.synchronize(self.device)
         with torch.cuda.graph(g, stream=stream):
-            self.step(partial_fn)
-            self.step(partial_fn)
+            for _ in range(2):
+                if delivered:
+                    self.step_delivered(partial_fn)
+                else:
+                    self.step(partial_fn)
         self.steps -= 2   # they run when the graph is replayed
         return g
 

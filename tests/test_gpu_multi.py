@@ -1,10 +1,16 @@
-"""The sequence split's fused NVLink exchange + merge kernel (kvr_exchange_merge).
+"""The sequence split's fused NVLink exchange + merge kernels
+(kvr_exchange_merge, and the delivered mode: kvr_decode_partial_exchange +
+kvr_exchange_merge_delivered).
 
 On one GPU: the kernel's time-limited wait for a peer that never signals
-runs out, sets the error flag and returns, and the next step completes.
+runs out, sets the error flag and returns, and the next step completes; the
+delivered mode with two ranks emulated on one GPU (every launch serialised
+on one stream, so each wait finds its flags already set) stores each rank's
+partials bit-identical to kvr_decode_partial and merges bit-identical to
+kvr_lse_merge.
 On two GPUs (skipped with fewer): the split against the single-GPU decode of
 the whole sequence, eagerly and as the replayed CUDA graph the benchmark
-times, at the benchmarked 28-layer 32K shape.
+times, at the benchmarked 28-layer 32K shape, in both modes.
 """
 import ctypes
 import os
@@ -23,7 +29,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result, seq_len, layers, graph_steps):
+def _worker(rank, world, port, result, seq_len, layers, graph_steps, delivered):
     import torch.distributed as dist
 
     import kv_reduce_b200 as kvr
@@ -56,7 +62,7 @@ def _worker(rank, world, port, result, seq_len, layers, graph_steps):
         ref = torch.cat([f.reshape(-1, wl.head_dim) for f in full])
         worst = 0.0
         for _ in range(4):   # both halves of the receive buffers, twice
-            out = xchg.step(launch.partial).float()
+            out = (xchg.step_delivered(launch) if delivered else xchg.step(launch.partial)).float()
             torch.cuda.synchronize()
             worst = max(worst, float((out - ref).abs().max()))
         if graph_steps:
@@ -64,7 +70,7 @@ def _worker(rank, world, port, result, seq_len, layers, graph_steps):
             side = torch.cuda.Stream(device)
             launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)],
                                     device, stream=side.cuda_stream)
-            graph = xchg.capture_pair(launch_g.partial, side)
+            graph = xchg.capture_pair(launch_g if delivered else launch_g.partial, side, delivered=delivered)
             for _ in range(graph_steps):
                 xchg.replay_pair(graph)
                 torch.cuda.synchronize()
@@ -78,15 +84,16 @@ def _worker(rank, world, port, result, seq_len, layers, graph_steps):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("delivered", [False, True], ids=["push", "delivered"])
 @pytest.mark.parametrize("seq_len,layers,graph_steps", [(5000, 3, 0), (32768, 28, 3)])
-def test_two_gpu_sequence_split_fused_exchange(built_lib, seq_len, layers, graph_steps):
+def test_two_gpu_sequence_split_fused_exchange(built_lib, seq_len, layers, graph_steps, delivered):
     import torch.multiprocessing as mp
 
     world = 2
     with mp.get_context("spawn").Manager() as manager:
         result = manager.dict()
-        mp.spawn(_worker, args=(world, _free_port(), result, seq_len, layers, graph_steps), nprocs=world,
-                 join=True)
+        mp.spawn(_worker, args=(world, _free_port(), result, seq_len, layers, graph_steps, delivered),
+                 nprocs=world, join=True)
         for rank in range(world):
             worst, errors, scale = result[rank]
             assert errors == 0
@@ -157,3 +164,111 @@ def test_exchange_wait_times_out_without_peer(built_lib):
     assert state[2].item() == 0 and state[0].item() == 2
     expect = o / ml[:, 1:2]
     assert torch.allclose(out.float(), expect, rtol=2.0 ** -8, atol=1e-6)
+
+
+def test_delivered_exchange_two_ranks_on_one_gpu(built_lib):
+    """Delivered mode, world 2 emulated on one GPU.  Both receive buffers and
+    both ranks' exchange state are local; the launches run in order on one
+    stream (decode rank 0, decode rank 1, merge rank 0, merge rank 1), so
+    every word a merge waits for was written by a decode that has already
+    completed.  Per step: each rank's slot in BOTH receive areas, as
+    (value, epoch) words is bit-identical to kvr_decode_partial over its
+    shard, every word carries the step's epoch, both merges are
+    bit-identical to kvr_lse_merge of the two partials, and the result is
+    the single-GPU decode of the whole sequence within the bf16 bound.
+    Then one rank skips a step and the other's bounded wait runs out."""
+    import kv_reduce_b200 as kvr
+    from kv_reduce_b200 import _lib
+    from kv_reduce_b200 import distributed as kd
+    from kv_reduce_b200 import workloads
+    from kv_reduce_b200.packed_kv_attention import DecodeLaunch, _geometry, _layer_ptrs
+
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    world = 2
+    wl = workloads.CONFIGS["2"].scaled(seq_len=5000, layers=3)
+    D = wl.head_dim
+    rows = wl.layers * wl.batch * wl.q_heads
+    shards = kd.token_shards(wl.seq_len, world, align=wl.group_size)
+    launches, full, keep = [], [], []
+    per_rank = [([], [], []) for _ in range(world)]
+    for layer in range(wl.layers):
+        k, v = workloads.make_layer_kv(wl, layer, device="cuda")
+        pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+        q = workloads.make_query(wl, layer, device="cuda")
+        full.append(kvr.packed_kv_decode_attention(q, pk, pv, out_dtype=torch.float32))
+        for r, (a, b) in enumerate(shards):
+            sk, sv = kd.shard_component(pk, pv, a, b)
+            assert torch.equal(sk.scale_pairs, kvr.key_scale_pairs(sk.scale, 4))
+            per_rank[r][0].append(sk), per_rank[r][1].append(sv), per_rank[r][2].append(q)
+    for ks, vs, qs in per_rank:
+        dummy = [torch.empty_like(q) for q in qs]
+        keep.append(dummy)
+        launches.append(DecodeLaunch(_geometry(qs[0], ks[0], vs[0]),
+                                     [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], dev))
+    ref = torch.cat([f.reshape(-1, D) for f in full])
+    # each rank's partials from the plain partial entry point
+    parts = []
+    for ln in launches:
+        ml = torch.empty(rows, 2, dtype=torch.float32, device="cuda")
+        o = torch.empty(rows, D, dtype=torch.float32, device="cuda")
+        ln.partial(ml, o)
+        parts.append((ml, o))
+    merged = kvr.lse_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]))
+
+    slot = rows * (2 + D)
+    data_floats = 2 * world * slot
+    bufs = [torch.zeros(data_floats + 64 + 2 * data_floats, dtype=torch.float32, device="cuda")
+            for _ in range(world)]
+    recv = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    signal = recv + data_floats * 4
+    states = [torch.zeros(4, dtype=torch.int32, device="cuda") for _ in range(world)]
+    outs = [torch.empty(rows, D, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+
+    def xargs(r, timeout_ns=1_000_000_000):
+        st = states[r].data_ptr()
+        return _lib.ExchangeArgs(world, r, rows, D, recv.data_ptr(), signal.data_ptr(), st, st + 4, st + 8,
+                                 outs[r].data_ptr(), timeout_ns)
+
+    args = [xargs(r) for r in range(world)]
+    stream = torch.cuda.current_stream().cuda_stream
+    for step in range(1, 5):   # both receive halves, twice
+        for r, ln in enumerate(launches):
+            assert lib.kvr_decode_partial_exchange(ln.args, ln.token_begin, ln.token_end, ctypes.byref(args[r]),
+                                                   stream) == _lib.KVR_OK
+        for r in range(world):
+            assert lib.kvr_exchange_merge_delivered(ctypes.byref(args[r]), stream) == _lib.KVR_OK
+        torch.cuda.synchronize()
+        par = step & 1
+        for r in range(world):
+            assert states[r][2].item() == 0, "a wait timed out"
+            assert states[r][0].item() == step and states[r][1].item() == 0
+            words = bufs[r].view(torch.int32)[data_floats + 64:].view(2, world, rows, 2 + D, 2)
+            for src in range(world):
+                w = words[par, src]
+                assert bool((w[..., 1] == step).all()), "a word does not carry the step's epoch"
+                assert torch.equal(w[:, :2, 0], parts[src][0].view(torch.int32)), (step, r, src)
+                assert torch.equal(w[:, 2:, 0], parts[src][1].view(torch.int32)), (step, r, src)
+            assert torch.equal(outs[r], merged), (step, r)
+        err = (outs[0].float() - ref).abs().max().item()
+        assert err <= 2e-3 + ref.abs().max().item() * 2.0 ** -8, err
+    # rank 1 does not take step 5: rank 0's merge finds rank 1's words still
+    # tagged with step 3, its 50 ms wait runs out, the error flag is raised
+    # and the kernel returns
+    short = xargs(0, 50_000_000)
+    ln = launches[0]
+    assert lib.kvr_decode_partial_exchange(ln.args, ln.token_begin, ln.token_end, ctypes.byref(short),
+                                           stream) == _lib.KVR_OK
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert lib.kvr_exchange_merge_delivered(ctypes.byref(short), stream) == _lib.KVR_OK
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert states[0][2].item() == 1, "the time-out did not raise the error flag"
+    assert states[0][0].item() == 5 and states[0][1].item() == 0
+    assert 0.04 <= waited < 5.0, waited
+    # the exchange's rows must be the launch's layers x batch x q_heads
+    bad = _lib.ExchangeArgs(world, 0, rows + 1, D, recv.data_ptr(), signal.data_ptr(), states[0].data_ptr(),
+                            states[0].data_ptr() + 4, states[0].data_ptr() + 8, outs[0].data_ptr(), 1)
+    assert lib.kvr_decode_partial_exchange(launches[0].args, launches[0].token_begin, launches[0].token_end,
+                                           ctypes.byref(bad), stream) == _lib.KVR_ERR_INVALID_ARGUMENT
