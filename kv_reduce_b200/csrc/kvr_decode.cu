@@ -1019,9 +1019,9 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     // cluster (from_cluster), from the shared memory of the cluster's CTAs:
     // partial s is CTA s's cpart.  The source is a compile-time choice so
     // the global merge keeps all its loads in flight before the first use.
-    auto merge = [&](auto from_cluster, const float* src, int n, float* dst) {
+    auto merge = [&](auto from_cluster, const float* src, int n, float* dst, int h0, int h_step) {
       constexpr bool DSM = decltype(from_cluster)::value;
-      for (int h = warp; h < gqa; h += kWarps) {
+      for (int h = h0; h < gqa; h += h_step) {
         const int d = 4 * lane;
         const bool dl = d < D;
         float ms[kFan], ls[kFan];
@@ -1066,11 +1066,13 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     };
     if (clustered) {
       // Cluster merge (the cluster is all NS splits of this unit): every
-      // CTA's partial sits in its own shared memory; rank 0 merges them over
-      // distributed shared memory straight into the output.  The second
-      // barrier keeps every CTA's shared memory alive until rank 0 has read it.
+      // CTA's partial sits in its own shared memory; the heads are dealt
+      // out over the cluster's CTAs and warps (head h to CTA h % NS), each
+      // merged over distributed shared memory straight into the output, so
+      // the merge and its output stores are spread over NS SMs.  The second
+      // barrier keeps every CTA's shared memory alive until all have read it.
       cluster_sync_all();
-      if (cluster_rank() == 0) merge(std::true_type{}, nullptr, NS, nullptr);
+      merge(std::true_type{}, nullptr, NS, nullptr, (int)cluster_rank() + NS * warp, NS * kWarps);
       cluster_sync_all();
       continue;
     }
@@ -1085,11 +1087,11 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     __threadfence();
     const float* src1 = p.part1 + ((int64_t)unit * NS + grp1 * kFan) * pstride;
     if (G1 == 1) {
-      merge(std::false_type{}, src1, n1, nullptr);
+      merge(std::false_type{}, src1, n1, nullptr, warp, kWarps);
       if (threadIdx.x == 0) p.cnt1[(int64_t)unit * G1 + grp1] = 0;
       continue;
     }
-    merge(std::false_type{}, src1, n1, p.part2 + ((int64_t)unit * G1 + grp1) * pstride);
+    merge(std::false_type{}, src1, n1, p.part2 + ((int64_t)unit * G1 + grp1) * pstride, warp, kWarps);
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1099,7 +1101,7 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     __syncthreads();
     if (!s_flag) continue;
     __threadfence();
-    merge(std::false_type{}, p.part2 + (int64_t)unit * G1 * pstride, G1, nullptr);
+    merge(std::false_type{}, p.part2 + (int64_t)unit * G1 * pstride, G1, nullptr, warp, kWarps);
     if (threadIdx.x == 0) p.cnt2[unit] = 0;
   }
 }
