@@ -484,8 +484,9 @@ def measure_split_sequence(args, wl, world, rank, device, mode="delivered"):
     (kv_reduce_b200.distributed.shard_component); a step is one partial
     decode launch over all layers of the shard and one exchange kernel.
     mode "delivered": the decode stores each finished row of (m, l, o)
-    partials into every peer over NVLink and releases a per-row flag; the
-    exchange kernel waits for the flags and merges.  "push": the decode
+    partials into every peer over NVLink as (value, epoch) words; the
+    exchange kernel reads them until every word carries the step's epoch,
+    and merges.  "push": the decode
     writes its partials locally; the exchange kernel stores them into every
     peer, signals and merges.  "nccl": an NCCL all-gather and the LSE merge
     kernel.  The step time is the max over ranks; the result counts the
@@ -574,7 +575,8 @@ def measure_split_sequence(args, wl, world, rank, device, mode="delivered"):
            "parallelism": f"token-split x{world}", "shard_tokens": b - a, "num_splits": launch.num_splits,
            "us_per_step": ms * 1e3, "gbps": value, "tokens_per_s": wl.batch / (ms * 1e-3),
            "frac_per_gpu": value / world / peak, "frac_note": "of measured, per GPU", "steps": n_steps,
-           "exchange": ("decode stores rows into the peers over NVLink + per-row flags; one wait-and-merge kernel"
+           "exchange": ("the decode stores its partial rows into every peer over NVLink as (value, epoch) "
+                        "words; one wait-and-merge kernel"
                         if p2p and delivered else
                         "one kernel: NVLink peer stores + signal + LSE merge" if p2p else
                         "NCCL all-gather + LSE merge launch" if world > 1 else "none"),

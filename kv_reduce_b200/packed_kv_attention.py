@@ -431,6 +431,7 @@ class PackedDecoder:
         self._q_step = head_dim * int(q_heads) * batch * 2
         self._o_step = head_dim * int(q_heads) * batch * (4 if out_dtype == torch.float32 else 2)
         self._bases = (0, 0)
+        self._host = None   # host_step's recorded graph and buffers
 
     @property
     def num_splits(self) -> int:
@@ -483,15 +484,17 @@ class PackedDecoder:
         addressing, kvr_host_mapped) the decode's final merge writes the
         outputs straight into it, otherwise a copy brings them back.  (Reading
         the queries the same way measured slower: every split of a (layer,
-        b, kv head) would fetch its query across PCIe.)  The first call with a
+        b, kv head) would fetch its query across PCIe; so did a copy kernel
+        reading them across PCIe ahead of the decode.)  The first call with a
         pair of buffers runs the step eagerly and records it as a CUDA graph
         on a private stream; every call replays that graph and waits for it.
         Returns ``out`` holding this step's outputs.  The host buffers must
         stay alive and in place; passing another pair records a new graph.
         """
-        key = (queries.data_ptr(), out.data_ptr(), tuple(queries.shape), queries.dtype, tuple(out.shape), out.dtype)
-        hs = getattr(self, "_host", None)
-        if hs is not None and hs["key"] == key:
+        hs = self._host
+        if (hs is not None and hs["q"] is queries and hs["o"] is out and queries.data_ptr() == hs["qp"]
+                and out.data_ptr() == hs["op"] and queries.shape == hs["shape"] and out.shape == hs["shape"]
+                and queries.dtype == torch.bfloat16 and out.dtype == self.out_dtype):
             hs["graph"].replay()
             torch.cuda.current_stream(self.device).synchronize()
             return out
@@ -531,7 +534,8 @@ class PackedDecoder:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             step()
-        self._host = {"key": key, "graph": graph, "buffers": (q_buf, o_buf, queries, out),
+        self._host = {"q": queries, "o": out, "qp": queries.data_ptr(), "op": out.data_ptr(),
+                      "shape": queries.shape, "graph": graph, "buffers": (q_buf, o_buf),
                       "launches": launches, "stream": stream, "zero_copy": zero_copy}
         return out
 

@@ -4,10 +4,11 @@ kvr_exchange_merge_delivered).
 
 On one GPU: the kernel's time-limited wait for a peer that never signals
 runs out, sets the error flag and returns, and the next step completes; the
-delivered mode with two ranks emulated on one GPU (every launch serialised
-on one stream, so each wait finds its flags already set) stores each rank's
-partials bit-identical to kvr_decode_partial and merges bit-identical to
-kvr_lse_merge.
+delivered mode with 2, 3 and 8 ranks emulated on one GPU (every launch
+serialised on one stream, so each wait finds its words already written)
+stores each rank's partials bit-identical to kvr_decode_partial and merges
+bit-identical to kvr_lse_merge, and its wait for ranks that skip a step
+runs out the same way.
 On two GPUs (skipped with fewer): the split against the single-GPU decode of
 the whole sequence, eagerly and as the replayed CUDA graph the benchmark
 times, at the benchmarked 28-layer 32K shape, in both modes.
@@ -166,17 +167,18 @@ def test_exchange_wait_times_out_without_peer(built_lib):
     assert torch.allclose(out.float(), expect, rtol=2.0 ** -8, atol=1e-6)
 
 
-def test_delivered_exchange_two_ranks_on_one_gpu(built_lib):
-    """Delivered mode, world 2 emulated on one GPU.  Both receive buffers and
-    both ranks' exchange state are local; the launches run in order on one
-    stream (decode rank 0, decode rank 1, merge rank 0, merge rank 1), so
-    every word a merge waits for was written by a decode that has already
-    completed.  Per step: each rank's slot in BOTH receive areas, as
-    (value, epoch) words is bit-identical to kvr_decode_partial over its
-    shard, every word carries the step's epoch, both merges are
-    bit-identical to kvr_lse_merge of the two partials, and the result is
-    the single-GPU decode of the whole sequence within the bf16 bound.
-    Then one rank skips a step and the other's bounded wait runs out."""
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
+    """Delivered mode, `world` ranks emulated on one GPU.  Every receive
+    buffer and every rank's exchange state is local; the launches run in
+    order on one stream (the decodes of ranks 0..world-1, then their
+    merges), so every word a merge waits for was written by a decode that
+    has already completed.  Per step: each rank's slot in EVERY receive
+    area, as (value, epoch) words, is bit-identical to kvr_decode_partial
+    over its shard, every word carries the step's epoch, every merge is
+    bit-identical to kvr_lse_merge of all partials, and the result is the
+    single-GPU decode of the whole sequence within the bf16 bound.  Then
+    rank 0 alone takes a step and its bounded wait for the others runs out."""
     import kv_reduce_b200 as kvr
     from kv_reduce_b200 import _lib
     from kv_reduce_b200 import distributed as kd
@@ -185,7 +187,6 @@ def test_delivered_exchange_two_ranks_on_one_gpu(built_lib):
 
     lib = _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device())
-    world = 2
     wl = workloads.CONFIGS["2"].scaled(seq_len=5000, layers=3)
     D = wl.head_dim
     rows = wl.layers * wl.batch * wl.q_heads
@@ -252,9 +253,9 @@ def test_delivered_exchange_two_ranks_on_one_gpu(built_lib):
             assert torch.equal(outs[r], merged), (step, r)
         err = (outs[0].float() - ref).abs().max().item()
         assert err <= 2e-3 + ref.abs().max().item() * 2.0 ** -8, err
-    # rank 1 does not take step 5: rank 0's merge finds rank 1's words still
-    # tagged with step 3, its 50 ms wait runs out, the error flag is raised
-    # and the kernel returns
+    # the other ranks do not take step 5: rank 0's merge finds their words
+    # still tagged with step 3, its 50 ms wait runs out, the error flag is
+    # raised and the kernel returns
     short = xargs(0, 50_000_000)
     ln = launches[0]
     assert lib.kvr_decode_partial_exchange(ln.args, ln.token_begin, ln.token_end, ctypes.byref(short),
