@@ -220,6 +220,13 @@ typedef struct {
   int num_sms;        /* 0: query the current device */
   void* workspace; size_t workspace_bytes;   /* split partials */
   int* counters;      /* n_layers*batch*kv_heads ints, zero on entry */
+  /* 1: the layers' query pointers are page-locked host memory the device
+   * addresses directly (kvr_host_mapped).  Where the launch runs in
+   * clusters (kvr_decode_cluster > 1) one CTA per (layer, b, kv head)
+   * reads its queries across PCIe and shares them with the other splits
+   * over distributed shared memory; otherwise every split reads them.
+   * Zero-initialise the struct so the field is 0 when unused.              */
+  int query_host_mapped;
 } kvr_decode_args;
 
 /* Key scales as fp16 pairs in the decode kernel's register order, for
@@ -252,6 +259,10 @@ int kvr_decode_nonfinite(int* flag, int clear);
 int kvr_decode_plan(const kvr_decode_args* a, int* num_splits,
                     size_t* workspace_bytes, size_t* counter_count);
 int kvr_decode_attention(const kvr_decode_args* a, kvr_stream_t stream);
+/* The cluster size kvr_decode_attention would launch with on the current
+ * device (1: no clusters; > 1: all splits of a (layer, b, kv head) form one
+ * cluster).  No reference counterpart.                                     */
+int kvr_decode_cluster(const kvr_decode_args* a, int* cluster);
 
 /* Same as kvr_decode_attention for callers that cannot allocate device
  * memory (an FFI host without a CUDA allocator, a serving loop that must not

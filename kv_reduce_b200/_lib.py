@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "kvr_append",
     "kvr_flush_groups",
     "kvr_decode_plan",
+    "kvr_decode_cluster",
     "kvr_decode_attention",
     "kvr_decode_attention_simt",
     "kvr_decode_simt_workspace",
@@ -162,7 +163,7 @@ class DecodeArgs(Structure):
         ("value_meta_bh_stride", c_int64),
         ("out_dtype", c_int), ("split_tokens", c_int), ("num_sms", c_int),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
-        ("counters", c_void_p),
+        ("counters", c_void_p), ("query_host_mapped", c_int),
     ]
 
 
@@ -192,6 +193,7 @@ def load() -> ctypes.CDLL:
     lib.kvr_append.argtypes = [POINTER(AppendArgs), c_void_p]
     lib.kvr_flush_groups.argtypes = [POINTER(FlushArgs), c_void_p]
     lib.kvr_decode_plan.argtypes = [POINTER(DecodeArgs), POINTER(c_int), POINTER(c_size_t), POINTER(c_size_t)]
+    lib.kvr_decode_cluster.argtypes = [POINTER(DecodeArgs), POINTER(c_int)]
     lib.kvr_decode_attention.argtypes = [POINTER(DecodeArgs), c_void_p]
     lib.kvr_decode_partial.argtypes = [POINTER(DecodeArgs), c_int, c_int, c_void_p, c_void_p, c_void_p]
     lib.kvr_lse_merge.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]

@@ -129,6 +129,7 @@ struct Params {
   int* dev_len;                  // non-null: sequence / prefix length read here at run time
   int res_cap;                   // residual rows the key residual buffer holds
   int cluster;                   // > 1: launched in clusters of NS CTAs, one per unit
+  int q_shared;                  // queries in host-mapped memory: in a cluster, rank 0 alone reads them
   // fused append of one new token per (b, kv head) before the decode
   // (device-side lengths only): its key row goes to the BF16 residual, its
   // value row is quantized per token, and the sequence length advances
@@ -630,7 +631,12 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
     // while the first chunks are in flight.  Lane (g, t4): words [0, D/8)
     // are fp16x2 (q[d(r,0)], q[d(r,1)]) / f_r in key-register order, words
     // [D/8, D/4) the raw bf16 pairs of q[dbase .. dbase + D/4).
-    if (warp == 0) {
+    // Queries in host-mapped memory, clustered plan (one item per CTA, the
+    // cluster = the unit's splits): rank 0 alone reads them across PCIe and
+    // stages them; the other CTAs copy its staged words over distributed
+    // shared memory, so each query crosses PCIe once, not once per split.
+    const bool q_from_rank0 = p.q_shared && NS > 1 && p.cluster > 1;
+    if (warp == 0 && !(q_from_rank0 && cluster_rank() != 0)) {
       uint32_t raw[D / 8];
       float amax = 0.f;
 #pragma unroll
@@ -671,6 +677,19 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
           w[k] = pack_half2(q0, q1);
         }
         qs[v * 32 + lane] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    if (q_from_rank0) {
+      cluster_sync_all();   // rank 0's staged query and exponent are written and visible
+      if (cluster_rank() != 0) {
+        // rank 0 keeps them unchanged to the end of its item, and cannot end
+        // it before this CTA reaches the cluster merge's barrier
+        const uint32_t src = dsmem_map(smem_u32(qs), 0);
+        for (int i = threadIdx.x; i < C::QS_BYTES / 16; i += blockDim.x) {
+          const float4 v = dsmem_f32x4(src + 16 * i);
+          qs[i] = make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w));
+        }
+        if (threadIdx.x == 0) s_qexp = __float_as_int(dsmem_f32(dsmem_map(smem_u32(&s_qexp), 0)));
       }
     }
     __syncthreads();
@@ -1293,6 +1312,7 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   p.dev_len = nullptr;
   p.res_cap = a->seq_len - a->prefix_len;
   p.cluster = pl.cluster;
+  p.q_shared = a->query_host_mapped ? 1 : 0;
   p.app_k = nullptr;
   p.app_v = nullptr;
   p.x_signal = nullptr;
@@ -1409,7 +1429,14 @@ static int run_t(const kvr_decode_args* a, int tb, int te, float* out_ml, float*
     occ = std::max(1, std::min(C::MIN_CTAS, (228 * 1024) / (C::SMEM + 1024)));
   }
   Plan pl = cached_plan(a, tb, te, occ);
-  if (plan_only) { *plan_only = pl; return KVR_OK; }
+  if (plan_only) {
+    if (dev_st == KVR_OK)
+      pl.cluster = x                     ? cluster_for<D, KB, VB, KVR_MAX_LAYERS, true>(pl)
+                   : (a->n_layers == 1) ? cluster_for<D, KB, VB, 1>(pl)
+                                        : cluster_for<D, KB, VB, KVR_MAX_LAYERS>(pl);
+    *plan_only = pl;
+    return KVR_OK;
+  }
   if (pl.num_splits > 1) {
     if (!a->workspace || a->workspace_bytes < pl.part_bytes || !a->counters) return KVR_ERR_WORKSPACE;
     if (!aligned16(a->workspace)) return KVR_ERR_MISALIGNED;
@@ -1473,6 +1500,15 @@ extern "C" int kvr_decode_plan(const kvr_decode_args* a, int* num_splits, size_t
   if (num_splits) *num_splits = pl.num_splits;
   if (workspace_bytes) *workspace_bytes = pl.part_bytes;
   if (counter_count) *counter_count = pl.counters;
+  return KVR_OK;
+}
+
+extern "C" int kvr_decode_cluster(const kvr_decode_args* a, int* cluster) {
+  if (!a || !cluster) return KVR_ERR_INVALID_ARGUMENT;
+  dec::Plan pl;
+  int st = dec::run(a, 0, a->seq_len, nullptr, nullptr, nullptr, &pl);
+  if (st != KVR_OK) return st;
+  *cluster = pl.cluster;
   return KVR_OK;
 }
 

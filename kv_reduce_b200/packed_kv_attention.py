@@ -244,6 +244,15 @@ class DecodeLaunch:
     def __call__(self) -> None:
         _lib.check("kvr_decode_attention", _lib.load().kvr_decode_attention(self.args, self.stream))
 
+    @property
+    def cluster(self) -> int:
+        """Cluster size of the launch on this device (kvr_decode_cluster):
+        1, or the split count when each (layer, b, kv head)'s splits form one
+        thread-block cluster."""
+        n = ctypes.c_int(1)
+        _lib.check("kvr_decode_cluster", _lib.load().kvr_decode_cluster(self.args, ctypes.byref(n)))
+        return int(n.value)
+
     def partial(self, part_ml: torch.Tensor, part_o: torch.Tensor) -> None:
         """Unnormalised (m, l, o) over tokens [token_begin, token_end)."""
         _lib.check("kvr_decode_partial", _lib.load().kvr_decode_partial(
@@ -479,13 +488,16 @@ class PackedDecoder:
         are read there (a CPU-side draft controller, a caller that keeps no
         device buffers of its own).  ``queries`` and ``out`` are pinned host
         tensors of the step's shape ([L, B, HQ, 1, D]; bf16 and the decoder's
-        output dtype).  The step copies the queries in (one copy); when the
-        GPU addresses ``out`` directly (pinned memory under unified
-        addressing, kvr_host_mapped) the decode's final merge writes the
-        outputs straight into it, otherwise a copy brings them back.  (Reading
-        the queries the same way measured slower: every split of a (layer,
-        b, kv head) would fetch its query across PCIe; so did a copy kernel
-        reading them across PCIe ahead of the decode.)  The first call with a
+        output dtype).  When the GPU addresses ``out`` directly (pinned memory
+        under unified addressing, kvr_host_mapped) the decode's final merge
+        writes the outputs straight into it, otherwise a copy brings them
+        back.  Mapped queries are read in place when every launch runs in
+        thread-block clusters (kvr_decode_cluster): one CTA per (layer, b, kv
+        head) reads them across PCIe and shares them with the other splits
+        over distributed shared memory (query_host_mapped); otherwise the
+        step copies them in (one copy).  (Every split reading its own query
+        across PCIe measured slower than the copy, and so did a copy kernel
+        reading them ahead of the decode.)  The first call with a
         pair of buffers runs the step eagerly and records it as a CUDA graph
         on a private stream; every call replays that graph and waits for it.
         Returns ``out`` holding this step's outputs.  The host buffers must
@@ -506,22 +518,39 @@ class PackedDecoder:
             raise ValueError(f"out must be a contiguous pinned host {self.out_dtype} tensor of shape {self.q_shape}.")
         self._host = None
         zero_copy = _lib.host_mapped(out.data_ptr())   # outputs written in place
-        q_buf = torch.empty(self.q_shape, dtype=torch.bfloat16, device=self.device)
         o_buf = out if zero_copy else torch.empty(self.q_shape, dtype=self.out_dtype, device=self.device)
         stream = torch.cuda.Stream(self.device)
-        layers = []
-        for i, layer in enumerate(self._layers):
-            copy = _lib.LayerPtrs.from_buffer_copy(layer)
-            copy.query = q_buf.data_ptr() + i * self._q_step
-            copy.out = o_buf.data_ptr() + i * self._o_step
-            layers.append(copy)
-        launches = [DecodeLaunch(self.geom, layers[s:s + _lib.KVR_MAX_LAYERS], self.device,
+
+        def make_launches(q_base: int) -> List[DecodeLaunch]:
+            layers = []
+            for i, layer in enumerate(self._layers):
+                copy = _lib.LayerPtrs.from_buffer_copy(layer)
+                copy.query = q_base + i * self._q_step
+                copy.out = o_buf.data_ptr() + i * self._o_step
+                layers.append(copy)
+            return [DecodeLaunch(self.geom, layers[s:s + _lib.KVR_MAX_LAYERS], self.device,
                                  split_tokens=self.split_tokens, stream=stream.cuda_stream,
                                  out_fp32=self.out_dtype == torch.float32)
                     for s in range(0, self.n_layers, _lib.KVR_MAX_LAYERS)]
 
+        # mapped queries read in place when every launch runs in clusters
+        # (one read per (layer, b, kv head), shared over distributed shared
+        # memory); otherwise one H2D copy into a device buffer per step
+        q_buf = None
+        launches = []
+        if _lib.host_mapped(queries.data_ptr()):
+            launches = make_launches(queries.data_ptr())
+            for launch in launches:
+                launch.args.query_host_mapped = 1
+            if not all(launch.cluster > 1 for launch in launches):
+                launches = []
+        if not launches:
+            q_buf = torch.empty(self.q_shape, dtype=torch.bfloat16, device=self.device)
+            launches = make_launches(q_buf.data_ptr())
+
         def step():
-            q_buf.copy_(queries, non_blocking=True)
+            if q_buf is not None:
+                q_buf.copy_(queries, non_blocking=True)
             for launch in launches:
                 launch()
             if not zero_copy:
@@ -536,7 +565,8 @@ class PackedDecoder:
             step()
         self._host = {"q": queries, "o": out, "qp": queries.data_ptr(), "op": out.data_ptr(),
                       "shape": queries.shape, "graph": graph, "buffers": (q_buf, o_buf),
-                      "launches": launches, "stream": stream, "zero_copy": zero_copy}
+                      "launches": launches, "stream": stream, "zero_copy": zero_copy,
+                      "queries_in_place": q_buf is None}
         return out
 
 

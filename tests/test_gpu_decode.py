@@ -325,6 +325,52 @@ def test_packed_decoder_host_step(kvr, layers, out_dtype):
         dec.host_step(torch.empty(dec.q_shape, dtype=torch.bfloat16), o_host)
 
 
+@pytest.mark.parametrize("split_tokens", [0, 128])
+def test_host_mapped_queries(kvr, split_tokens):
+    """Queries in pinned host memory, read by the decode in place
+    (kvr_decode_args.query_host_mapped): with the automatic plan the launch
+    runs in clusters and only rank 0 of each cluster reads the query (the
+    others copy its staged words over distributed shared memory); with
+    128-token splits (32 splits, no clusters) every split reads it.  Both
+    are bit-identical to the decode of the same queries in device memory.
+    host_step reads mapped queries in place when its launches are clustered."""
+    from kv_reduce_b200 import workloads
+    from kv_reduce_b200.packed_kv_attention import DecodeLaunch, _geometry, _layer_ptrs
+
+    wl = workloads.CONFIGS["2"].scaled(seq_len=4096, layers=4)
+    ks, vs, qs = [], [], []
+    for layer in range(wl.layers):
+        k, v = workloads.make_layer_kv(wl, layer)
+        pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=128)
+        ks.append(pk), vs.append(pv), qs.append(workloads.make_query(wl, layer))
+    q_host = [q.cpu().pin_memory() for q in qs]
+    dev = qs[0].device
+    geom = _geometry(qs[0], ks[0], vs[0])
+    o_dev = [torch.full_like(q, float("nan")) for q in qs]
+    o_map = [torch.full_like(q, float("nan")) for q in qs]
+    ref_l = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, o_dev, ks, vs)], dev,
+                         split_tokens=split_tokens)
+    lps = [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, o_map, ks, vs)]
+    for lp, qh in zip(lps, q_host):
+        lp.query = qh.data_ptr()
+    map_l = DecodeLaunch(geom, lps, dev, split_tokens=split_tokens)
+    map_l.args.query_host_mapped = 1
+    ref_l()
+    map_l()
+    torch.cuda.synchronize()
+    assert (map_l.cluster > 1) == (split_tokens == 0), (map_l.cluster, map_l.num_splits)
+    for a, b in zip(o_map, o_dev):
+        assert torch.equal(a, b)
+    if split_tokens == 0:
+        dec = kvr.PackedDecoder(ks, vs, q_heads=wl.q_heads)
+        qh = torch.stack(qs).cpu().pin_memory()
+        oh = torch.empty_like(qh).pin_memory()
+        for _ in range(2):
+            dec.host_step(qh, oh)
+        assert dec._host["queries_in_place"]
+        assert torch.equal(oh, dec(torch.stack(qs)).cpu())
+
+
 def test_cache_on_another_device_is_rejected(kvr):
     k, v, q = make((1, 2, 256, 128), 12, 4, 4, 32, 0, seed=2)
     pk, pv = kvr.pack_kivi_kv(k, v, k_bits=4, v_bits=4, group_size=32, residual_length=0)
