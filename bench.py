@@ -70,10 +70,11 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--exchange", choices=["delivered", "push", "nccl"], default="delivered",
+    p.add_argument("--exchange", choices=["delivered", "owner", "push", "nccl"], default="delivered",
                    help="sequence split's exchange: the decode stores its rows into the peers and one kernel "
-                        "waits and merges (delivered), one kernel pushes, signals and merges (push), or an "
-                        "NCCL all-gather plus the LSE merge launch (nccl)")
+                        "waits and merges (delivered); the decode stores each row into its owner rank, which "
+                        "merges it and sends the merged row to every rank (owner); one kernel pushes, signals "
+                        "and merges (push); or an NCCL all-gather plus the LSE merge launch (nccl)")
     p.add_argument("--nccl-exchange", action="store_true", help="same as --exchange nccl")
     p.add_argument("--draft-loop", action="store_true",
                    help="speculative draft loop on the streaming cache (use with --config 5)")
@@ -519,13 +520,14 @@ def measure_split_sequence(args, wl, world, rank, device, mode="delivered"):
                           split_tokens=args.split_tokens)
     out = torch.empty(rows, wl.head_dim, dtype=torch.bfloat16, device=device)
     p2p = world > 1 and mode != "nccl"
-    delivered = mode == "delivered"
+    delivered = mode in ("delivered", "owner")
+    owner = mode == "owner"
     if p2p:
         xchg = kd.PeerExchange(rows, wl.head_dim, device)
 
         def step():
             if delivered:
-                xchg.step_delivered(launch)
+                xchg.step_delivered(launch, owner=owner)
             else:
                 xchg.step(launch.partial)
     else:
@@ -545,7 +547,8 @@ def measure_split_sequence(args, wl, world, rank, device, mode="delivered"):
         side = torch.cuda.Stream(device)
         launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)], device,
                                 split_tokens=args.split_tokens, stream=side.cuda_stream)
-        graph = xchg.capture_pair(launch_g if delivered else launch_g.partial, side, delivered=delivered)
+        graph = xchg.capture_pair(launch_g if delivered else launch_g.partial, side, delivered=delivered,
+                                  owner=owner)
         for _ in range(2):
             xchg.replay_pair(graph)
         torch.cuda.synchronize()
@@ -575,7 +578,10 @@ def measure_split_sequence(args, wl, world, rank, device, mode="delivered"):
            "parallelism": f"token-split x{world}", "shard_tokens": b - a, "num_splits": launch.num_splits,
            "us_per_step": ms * 1e3, "gbps": value, "tokens_per_s": wl.batch / (ms * 1e-3),
            "frac_per_gpu": value / world / peak, "frac_note": "of measured, per GPU", "steps": n_steps,
-           "exchange": ("the decode stores its partial rows into every peer over NVLink as (value, epoch) "
+           "exchange": ("the decode stores each partial row into its owner rank over NVLink as (value, epoch) "
+                        "words; the owner merges it and stores the merged bf16 row into every rank; a gather "
+                        "kernel collects them" if p2p and owner else
+                        "the decode stores its partial rows into every peer over NVLink as (value, epoch) "
                         "words; one wait-and-merge kernel"
                         if p2p and delivered else
                         "one kernel: NVLink peer stores + signal + LSE merge" if p2p else
@@ -585,7 +591,8 @@ def measure_split_sequence(args, wl, world, rank, device, mode="delivered"):
                       if graph is not None else
                       "eager: partial decode (all layers, one launch) + exchange/merge per step")
                      + ", CUDA events, max over ranks",
-           "gpu_launches": n_steps * 2, "clocks": clocks.summary()}
+           "exchange_mode": mode if world > 1 else "none",
+           "gpu_launches": n_steps * (3 if p2p and owner else 2), "clocks": clocks.summary()}
     del graph
     if p2p:
         xchg.close()

@@ -350,6 +350,7 @@ typedef struct {
   int* error;           /* this rank, device: non-zero after a wait timed out */
   uint16_t* out;        /* bf16 [rows, head_dim] */
   long long timeout_ns;
+  int mode;             /* kvr_decode_partial_exchange: 0 rows to every rank, 1 rows to their owner */
 } kvr_exchange_args;
 int kvr_exchange_merge(const kvr_exchange_args* a, kvr_stream_t stream);
 
@@ -370,6 +371,21 @@ int kvr_exchange_merge(const kvr_exchange_args* a, kvr_stream_t stream);
 int kvr_decode_partial_exchange(const kvr_decode_args* a, int token_begin, int token_end,
                                 const kvr_exchange_args* x, kvr_stream_t stream);
 int kvr_exchange_merge_delivered(const kvr_exchange_args* a, kvr_stream_t stream);
+
+/* Owner mode (x->mode = 1; head_dim 64 or 128, world <= 8): a reduce-scatter
+ * of the partials, then an all-gather of the merged rows, both as tagged
+ * words.  kvr_decode_partial_exchange stores each row only into the
+ * receive area of its owner, rank row % world (same layout as above).
+ * kvr_exchange_merge_owned waits for every source's words of the rows this
+ * rank owns (bounded), merges them into out and stores each merged row as
+ * words (bf16 pair, epoch) into every peer's final area: uint32 words
+ * [2 halves][rows][D] after the receive area.  kvr_exchange_gather_owned
+ * then waits for the other ranks' rows there (bounded), copies them into
+ * out and advances the epoch.  Each rank sends about 1/world of the
+ * delivered mode's bytes, for one more hop.  The buffer of each rank is
+ * 8*world*rows*(2+D) + 256 + 16*world*rows*(2+D) + 8*rows*D bytes.         */
+int kvr_exchange_merge_owned(const kvr_exchange_args* a, kvr_stream_t stream);
+int kvr_exchange_gather_owned(const kvr_exchange_args* a, kvr_stream_t stream);
 
 /* Receive buffers shared between processes: device memory from cudaMalloc
  * (zeroed) with a 64-byte CUDA IPC handle; a peer maps it with

@@ -56,6 +56,8 @@ EXPORTED_SYMBOLS = (
     "kvr_decode_nonfinite",
     "kvr_exchange_merge",
     "kvr_exchange_merge_delivered",
+    "kvr_exchange_merge_owned",
+    "kvr_exchange_gather_owned",
     "kvr_decode_partial_exchange",
     "kvr_exchange_alloc",
     "kvr_exchange_open",
@@ -148,7 +150,7 @@ class ExchangeArgs(Structure):
     _fields_ = [
         ("world", c_int), ("rank", c_int), ("rows", c_int), ("head_dim", c_int),
         ("recv", c_void_p), ("signal", c_void_p), ("epoch", c_void_p), ("counter", c_void_p),
-        ("error", c_void_p), ("out", c_void_p), ("timeout_ns", ctypes.c_longlong),
+        ("error", c_void_p), ("out", c_void_p), ("timeout_ns", ctypes.c_longlong), ("mode", c_int),
     ]
 
 
@@ -210,6 +212,8 @@ def load() -> ctypes.CDLL:
     lib.kvr_decode_nonfinite.argtypes = [POINTER(c_int), c_int]
     lib.kvr_exchange_merge.argtypes = [POINTER(ExchangeArgs), c_void_p]
     lib.kvr_exchange_merge_delivered.argtypes = [POINTER(ExchangeArgs), c_void_p]
+    lib.kvr_exchange_merge_owned.argtypes = [POINTER(ExchangeArgs), c_void_p]
+    lib.kvr_exchange_gather_owned.argtypes = [POINTER(ExchangeArgs), c_void_p]
     lib.kvr_decode_partial_exchange.argtypes = [POINTER(DecodeArgs), c_int, c_int, POINTER(ExchangeArgs), c_void_p]
     lib.kvr_exchange_alloc.argtypes = [c_size_t, POINTER(c_void_p), ctypes.c_char_p]
     lib.kvr_exchange_open.argtypes = [ctypes.c_char_p, POINTER(c_void_p)]

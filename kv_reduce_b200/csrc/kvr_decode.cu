@@ -141,6 +141,7 @@ struct Params {
   int* const* x_signal;          // device array [x_world]: signal areas (receive areas at +kLLWords), or null
   const int* x_epoch;            // exchanges completed on this rank; this step is *x_epoch + 1
   int x_world, x_rank;
+  int x_owner;                   // 1: each row goes to its owner rank (row % x_world) only
 };
 constexpr int kLLWords = 64;     // 32-bit words of a signal area before its receive area
 
@@ -974,7 +975,10 @@ __global__ void __launch_bounds__(kWarps * 32, Cfg<D, KB, VB>::MIN_CTAS) decode_
           // for the stores to land (no fence, no flag)
           const uint32_t e = (uint32_t)x_e;
           const int64_t lslot = x_rows * (2 + D) * 2;   // 32-bit words per (half, source)
-          for (int r = 0; r < p.x_world; ++r) {
+          // owner mode: only the rank that merges this row receives it
+          const int r_lo = p.x_owner ? (int)(prow % p.x_world) : 0;
+          const int r_hi = p.x_owner ? r_lo + 1 : p.x_world;
+          for (int r = r_lo; r < r_hi; ++r) {
             uint32_t* base = reinterpret_cast<uint32_t*>(p.x_signal[r]) + kLLWords +
                              ((int64_t)(x_e & 1) * p.x_world + p.x_rank) * lslot + prow * (2 + D) * 2;
             st_volatile_v4(base + 2 * (2 + d), __float_as_uint(o.x), e, __float_as_uint(o.y), e);
@@ -1319,6 +1323,7 @@ static void fill_params(Params<MAXL>& p, const kvr_decode_args* a, const Plan& p
   p.x_epoch = nullptr;
   p.x_world = 0;
   p.x_rank = 0;
+  p.x_owner = 0;
 }
 
 // Per-device, per-instantiation set-up: dynamic shared memory limit and
@@ -1411,6 +1416,7 @@ static void set_exchange(Params<MAXL>& p, const kvr_exchange_args* x) {
   p.x_epoch = x->epoch;
   p.x_world = x->world;
   p.x_rank = x->rank;
+  p.x_owner = x->mode == 1 ? 1 : 0;
 }
 
 template <int D, int KB, int VB>

@@ -144,79 +144,154 @@ __device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* p) {
   return v;
 }
 
+// Merge of one row from the tagged words of every source at `area` (layout
+// [world sources][rows][2 + D][2] words): every source's (m, l) words and
+// this lane's four o words, all loads in flight at once; then only the words
+// whose tag is not yet e are read again, until the deadline (then
+// *timed_out is set and what is there is merged).  Returns this lane's four
+// bf16 outputs (d = 4 * lane) as two words, acc / L as in kvr_lse_merge, so
+// the two merges agree bit for bit.
+__device__ __forceinline__ uint2 merge_row(const uint32_t* area, int64_t lslot, int world, int row, int D,
+                                           uint32_t e, uint64_t deadline, bool* timed_out) {
+  const int lane = threadIdx.x & 31;
+  const int d = 4 * lane;
+  const bool dl = d < D;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  uint4 wml[8], wo0[8], wo1[8];
+  const uint4 zero = make_uint4(0u, e, 0u, e);
+#pragma unroll
+  for (int src = 0; src < 8; ++src) {
+    const uint32_t* r = area + src * lslot + (int64_t)row * (2 + D) * 2;
+    wml[src] = src < world ? ld_volatile_v4(r) : zero;
+    wo0[src] = (src < world && dl) ? ld_volatile_v4(r + 2 * (2 + d)) : zero;
+    wo1[src] = (src < world && dl) ? ld_volatile_v4(r + 2 * (2 + d) + 4) : zero;
+  }
+  for (;;) {
+    bool ready = true;
+#pragma unroll
+    for (int src = 0; src < 8; ++src) {
+      if (src >= world) break;
+      const uint32_t* r = area + src * lslot + (int64_t)row * (2 + D) * 2;
+      if (wml[src].y != e || wml[src].w != e) { ready = false; wml[src] = ld_volatile_v4(r); }
+      if (wo0[src].y != e || wo0[src].w != e) { ready = false; wo0[src] = ld_volatile_v4(r + 2 * (2 + d)); }
+      if (wo1[src].y != e || wo1[src].w != e) { ready = false; wo1[src] = ld_volatile_v4(r + 2 * (2 + d) + 4); }
+    }
+    if (ready || *timed_out) break;
+    if (global_timer_ns() > deadline) *timed_out = true;   // one more pass, then merge what is there
+  }
+  float M = NEG_INF;
+#pragma unroll
+  for (int src = 0; src < 8; ++src)
+    if (src < world) M = fmaxf(M, __uint_as_float(wml[src].x));
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float L = 0.f;
+#pragma unroll
+  for (int src = 0; src < 8; ++src) {
+    if (src >= world) break;
+    const float m = __uint_as_float(wml[src].x);
+    if (M == NEG_INF || m == NEG_INF) continue;
+    const float wt = exp2f(m - M);
+    acc.x = fmaf(wt, __uint_as_float(wo0[src].x), acc.x); acc.y = fmaf(wt, __uint_as_float(wo0[src].z), acc.y);
+    acc.z = fmaf(wt, __uint_as_float(wo1[src].x), acc.z); acc.w = fmaf(wt, __uint_as_float(wo1[src].z), acc.w);
+    L = fmaf(wt, __uint_as_float(wml[src].z), L);
+  }
+  const bool nz = L > 0.f;
+  uint2 pk;
+  pk.x = (uint32_t)f32_to_bf16_bits(nz ? acc.x / L : 0.f) | ((uint32_t)f32_to_bf16_bits(nz ? acc.y / L : 0.f) << 16);
+  pk.y = (uint32_t)f32_to_bf16_bits(nz ? acc.z / L : 0.f) | ((uint32_t)f32_to_bf16_bits(nz ? acc.w / L : 0.f) << 16);
+  return pk;
+}
+
+// The last CTA to arrive advances the epoch (every CTA read it first).
+__device__ __forceinline__ void advance_epoch(const kvr_exchange_args& a, int ep) {
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(a.counter, 1) == (int)gridDim.x - 1) {
+    *a.counter = 0;
+    *a.epoch = ep;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) merge_delivered_kernel(kvr_exchange_args a) {
   // launched as a programmatic dependent of this rank's decode: resident
   // early, but nothing is read before that decode has completed
   pdl_wait();
   const int world = a.world, rank = a.rank, rows = a.rows, D = a.head_dim;
   const int ep = *reinterpret_cast<volatile int*>(a.epoch) + 1;
-  const uint32_t e = (uint32_t)ep;
   const int64_t lslot = (int64_t)rows * (2 + D) * 2;   // words per (half, source)
   const uint32_t* area = reinterpret_cast<const uint32_t*>(a.signal[rank]) + kLLWords + (int64_t)(ep & 1) * world * lslot;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
   const int d = 4 * lane;
-  const bool dl = d < D;
   const uint64_t deadline = global_timer_ns() + (uint64_t)a.timeout_ns;
-  const float NEG_INF = -__int_as_float(0x7f800000);
   bool timed_out = false;
   for (int row = blockIdx.x * warps + warp; row < rows; row += gridDim.x * warps) {
-    // every source's (m, l) words and this lane's four o words, all loads
-    // in flight at once; then only the words whose tag is not yet this
-    // step's are read again, until the deadline
-    uint4 wml[8], wo0[8], wo1[8];
-    const uint4 zero = make_uint4(0u, e, 0u, e);
-#pragma unroll
-    for (int src = 0; src < 8; ++src) {
-      const uint32_t* r = area + src * lslot + (int64_t)row * (2 + D) * 2;
-      wml[src] = src < world ? ld_volatile_v4(r) : zero;
-      wo0[src] = (src < world && dl) ? ld_volatile_v4(r + 2 * (2 + d)) : zero;
-      wo1[src] = (src < world && dl) ? ld_volatile_v4(r + 2 * (2 + d) + 4) : zero;
-    }
-    for (;;) {
-      bool ready = true;
-#pragma unroll
-      for (int src = 0; src < 8; ++src) {
-        if (src >= world) break;
-        const uint32_t* r = area + src * lslot + (int64_t)row * (2 + D) * 2;
-        if (wml[src].y != e || wml[src].w != e) { ready = false; wml[src] = ld_volatile_v4(r); }
-        if (wo0[src].y != e || wo0[src].w != e) { ready = false; wo0[src] = ld_volatile_v4(r + 2 * (2 + d)); }
-        if (wo1[src].y != e || wo1[src].w != e) { ready = false; wo1[src] = ld_volatile_v4(r + 2 * (2 + d) + 4); }
-      }
-      if (ready || timed_out) break;
-      if (global_timer_ns() > deadline) timed_out = true;   // one more pass, then merge what is there
-    }
-    float M = NEG_INF;
-#pragma unroll
-    for (int src = 0; src < 8; ++src)
-      if (src < world) M = fmaxf(M, __uint_as_float(wml[src].x));
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float L = 0.f;
-#pragma unroll
-    for (int src = 0; src < 8; ++src) {
-      if (src >= world) break;
-      const float m = __uint_as_float(wml[src].x);
-      if (M == NEG_INF || m == NEG_INF) continue;
-      const float wt = exp2f(m - M);
-      acc.x = fmaf(wt, __uint_as_float(wo0[src].x), acc.x); acc.y = fmaf(wt, __uint_as_float(wo0[src].z), acc.y);
-      acc.z = fmaf(wt, __uint_as_float(wo1[src].x), acc.z); acc.w = fmaf(wt, __uint_as_float(wo1[src].z), acc.w);
-      L = fmaf(wt, __uint_as_float(wml[src].z), L);
-    }
-    if (dl) {
-      // acc / L as in kvr_lse_merge, so the two merges agree bit for bit
-      const bool nz = L > 0.f;
-      uint2 pk;
-      pk.x = (uint32_t)f32_to_bf16_bits(nz ? acc.x / L : 0.f) | ((uint32_t)f32_to_bf16_bits(nz ? acc.y / L : 0.f) << 16);
-      pk.y = (uint32_t)f32_to_bf16_bits(nz ? acc.z / L : 0.f) | ((uint32_t)f32_to_bf16_bits(nz ? acc.w / L : 0.f) << 16);
-      *reinterpret_cast<uint2*>(a.out + (int64_t)row * D + d) = pk;
-    }
+    const uint2 pk = merge_row(area, lslot, world, row, D, (uint32_t)ep, deadline, &timed_out);
+    if (d < D) *reinterpret_cast<uint2*>(a.out + (int64_t)row * D + d) = pk;
   }
   if (timed_out) atomicOr(a.error, 1);   // some row merged whatever was there: the output is invalid
-  // every CTA has read the epoch before it arrives; the last one advances it
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(a.counter, 1) == (int)gridDim.x - 1) {
-    *a.counter = 0;
-    *a.epoch = ep;
+  advance_epoch(a, ep);
+}
+
+// Owner mode, first kernel: the rows this rank owns (row % world == rank)
+// arrived from every rank (kvr_decode_partial_exchange with mode 1); merge
+// each, write it to out and store it, as tagged words (bf16 pair, epoch),
+// into every peer's final area: words [2 halves][rows][D] after the receive
+// area, a lane's four outputs as one 16-byte store.
+__global__ void __launch_bounds__(kThreads) merge_owned_kernel(kvr_exchange_args a) {
+  pdl_wait();
+  const int world = a.world, rank = a.rank, rows = a.rows, D = a.head_dim;
+  const int ep = *reinterpret_cast<volatile int*>(a.epoch) + 1;
+  const uint32_t e = (uint32_t)ep;
+  const int64_t lslot = (int64_t)rows * (2 + D) * 2;
+  const uint32_t* area = reinterpret_cast<const uint32_t*>(a.signal[rank]) + kLLWords + (int64_t)(ep & 1) * world * lslot;
+  const int64_t final_off = kLLWords + 2 * (int64_t)world * lslot + (int64_t)(ep & 1) * rows * D;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const int d = 4 * lane;
+  const int n_own = (rows - rank + world - 1) / world;
+  const uint64_t deadline = global_timer_ns() + (uint64_t)a.timeout_ns;
+  bool timed_out = false;
+  for (int j = blockIdx.x * warps + warp; j < n_own; j += gridDim.x * warps) {
+    const int row = rank + j * world;
+    const uint2 pk = merge_row(area, lslot, world, row, D, e, deadline, &timed_out);
+    if (d < D) {
+      *reinterpret_cast<uint2*>(a.out + (int64_t)row * D + d) = pk;
+      for (int r = 0; r < world; ++r) {
+        if (r == rank) continue;
+        uint32_t* f = reinterpret_cast<uint32_t*>(a.signal[r]) + final_off + (int64_t)row * D + d;
+        asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"l"(f), "r"(pk.x), "r"(e), "r"(pk.y),
+                     "r"(e) : "memory");
+      }
+    }
   }
+  if (timed_out) atomicOr(a.error, 1);
+}
+
+// Owner mode, second kernel: the rows other ranks own, read from this rank's
+// final area until every word carries this step's epoch (bounded), into
+// out; the last CTA advances the epoch.
+__global__ void __launch_bounds__(kThreads) gather_owned_kernel(kvr_exchange_args a) {
+  pdl_wait();
+  const int world = a.world, rank = a.rank, rows = a.rows, D = a.head_dim;
+  const int ep = *reinterpret_cast<volatile int*>(a.epoch) + 1;
+  const uint32_t e = (uint32_t)ep;
+  const int64_t lslot = (int64_t)rows * (2 + D) * 2;
+  const uint32_t* fin = reinterpret_cast<const uint32_t*>(a.signal[rank]) + kLLWords + 2 * (int64_t)world * lslot +
+                        (int64_t)(ep & 1) * rows * D;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const int d = 4 * lane;
+  const uint64_t deadline = global_timer_ns() + (uint64_t)a.timeout_ns;
+  bool timed_out = false;
+  for (int row = blockIdx.x * warps + warp; row < rows; row += gridDim.x * warps) {
+    if (row % world == rank || d >= D) continue;   // owned rows were written by merge_owned_kernel
+    const uint32_t* f = fin + (int64_t)row * D + d;
+    uint4 v = ld_volatile_v4(f);
+    while ((v.y != e || v.w != e) && !timed_out) {
+      if (global_timer_ns() > deadline) timed_out = true;
+      v = ld_volatile_v4(f);
+    }
+    *reinterpret_cast<uint2*>(a.out + (int64_t)row * D + d) = make_uint2(v.x, v.z);
+  }
+  if (timed_out) atomicOr(a.error, 1);
+  advance_epoch(a, ep);
 }
 
 }  // namespace xchg
@@ -289,5 +364,36 @@ extern "C" int kvr_exchange_merge_delivered(const kvr_exchange_args* a, kvr_stre
   constexpr int warps = xchg::kThreads / 32;
   const int grid = std::max(1, std::min(sms, (a->rows + warps - 1) / warps));
   (void)pdl_launch(xchg::merge_delivered_kernel, dim3(grid), dim3(xchg::kThreads), 0, as_stream(stream), 1, *a);
+  return check_launch();
+}
+
+static int check_owner_args(const kvr_exchange_args* a) {
+  if (!a || a->world < 1 || a->world > 8 || a->rank < 0 || a->rank >= a->world || a->rows < 1 ||
+      (a->head_dim != 64 && a->head_dim != 128) || !a->signal || !a->epoch || !a->counter || !a->out ||
+      !a->error || a->timeout_ns <= 0)
+    return KVR_ERR_INVALID_ARGUMENT;
+  return KVR_OK;
+}
+
+extern "C" int kvr_exchange_merge_owned(const kvr_exchange_args* a, kvr_stream_t stream) {
+  const int st = check_owner_args(a);
+  if (st != KVR_OK) return st;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  constexpr int warps = xchg::kThreads / 32;
+  const int n_own = (a->rows - a->rank + a->world - 1) / a->world;
+  const int grid = std::max(1, std::min(sms, (n_own + warps - 1) / warps));
+  (void)pdl_launch(xchg::merge_owned_kernel, dim3(grid), dim3(xchg::kThreads), 0, as_stream(stream), 1, *a);
+  return check_launch();
+}
+
+extern "C" int kvr_exchange_gather_owned(const kvr_exchange_args* a, kvr_stream_t stream) {
+  const int st = check_owner_args(a);
+  if (st != KVR_OK) return st;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  constexpr int warps = xchg::kThreads / 32;
+  const int grid = std::max(1, std::min(sms, (a->rows + warps - 1) / warps));
+  (void)pdl_launch(xchg::gather_owned_kernel, dim3(grid), dim3(xchg::kThreads), 0, as_stream(stream), 1, *a);
   return check_launch();
 }

@@ -170,7 +170,12 @@ class PeerExchange:
     (kvr_decode_partial_exchange), so the rows cross NVLink while the
     decode is still running and nothing is fenced; the exchange kernel
     (kvr_exchange_merge_delivered) reads the words until every one carries
-    the step's epoch, and merges.
+    the step's epoch, and merges.  ``step_delivered(launch, owner=True)``
+    sends each row only to its owner rank (row % world), which merges it
+    (kvr_exchange_merge_owned) and sends the merged bf16 row to every rank
+    as tagged words (kvr_exchange_gather_owned collects them): a
+    reduce-scatter and an all-gather, about 1/world of the bytes for one
+    more hop.
     """
 
     def __init__(self, rows: int, head_dim: int, device: torch.device, group=None,
@@ -187,9 +192,10 @@ class PeerExchange:
         slot = self.rows * (2 + self.head_dim)
         data_bytes = 2 * self.world * slot * 4
         ll_bytes = 2 * data_bytes   # delivered mode: (value, epoch) words after the signal area
+        final_bytes = 8 * self.rows * self.head_dim   # owner mode: merged rows as (bf16 pair, epoch) words
         own = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
-        _lib.call("kvr_exchange_alloc", data_bytes + 256 + ll_bytes, ctypes.byref(own), handle)
+        _lib.call("kvr_exchange_alloc", data_bytes + 256 + ll_bytes + final_bytes, ctypes.byref(own), handle)
         self._own = own.value
         mine = torch.tensor(list(handle.raw), dtype=torch.uint8, device=device)
         handles = torch.empty(self.world, 64, dtype=torch.uint8, device=device)
@@ -220,7 +226,9 @@ class PeerExchange:
         st = self.state.data_ptr()
         self._args = _lib.ExchangeArgs(self.world, self.rank, self.rows, self.head_dim, self.recv_ptrs.data_ptr(),
                                        self.signal_ptrs.data_ptr(), st, st + 4, st + 8, self.out.data_ptr(),
-                                       int(timeout_s * 1e9))
+                                       int(timeout_s * 1e9), 0)
+        self._args_owner = _lib.ExchangeArgs.from_buffer_copy(self._args)
+        self._args_owner.mode = 1
         self.steps = 0
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
@@ -235,10 +243,12 @@ class PeerExchange:
         self.steps = n
         return self.out
 
-    def step_delivered(self, launch) -> torch.Tensor:
+    def step_delivered(self, launch, owner: bool = False) -> torch.Tensor:
         """One step of the delivered mode on ``launch``'s stream: the decode
         over launch's token range with its rows stored into every rank's
-        receive buffer, then the wait-and-merge kernel."""
+        receive buffer, then the wait-and-merge kernel; with ``owner``, the
+        rows go to their owner ranks only, then the owner merge and the
+        gather of the merged rows."""
         import ctypes
 
         from . import _lib
@@ -246,18 +256,23 @@ class PeerExchange:
         if launch.geom.head_dim != self.head_dim or len(launch.layers) * launch.geom.batch * launch.geom.q_heads != self.rows:
             raise ValueError("the launch's rows (layers x batch x q_heads) and head_dim must match the exchange")
         lib = _lib.load()
+        x = self._args_owner if owner else self._args
         _lib.check("kvr_decode_partial_exchange", lib.kvr_decode_partial_exchange(
-            launch.args, launch.token_begin, launch.token_end, ctypes.byref(self._args), launch.stream))
-        _lib.check("kvr_exchange_merge_delivered", lib.kvr_exchange_merge_delivered(self._args, launch.stream))
+            launch.args, launch.token_begin, launch.token_end, ctypes.byref(x), launch.stream))
+        if owner:
+            _lib.check("kvr_exchange_merge_owned", lib.kvr_exchange_merge_owned(x, launch.stream))
+            _lib.check("kvr_exchange_gather_owned", lib.kvr_exchange_gather_owned(x, launch.stream))
+        else:
+            _lib.check("kvr_exchange_merge_delivered", lib.kvr_exchange_merge_delivered(x, launch.stream))
         self.steps += 1
         return self.out
 
     def capture_pair(self, partial_fn: Callable[[torch.Tensor, torch.Tensor], None],
-                     stream: torch.cuda.Stream, delivered: bool = False) -> torch.cuda.CUDAGraph:
+                     stream: torch.cuda.Stream, delivered: bool = False, owner: bool = False) -> torch.cuda.CUDAGraph:
         """Record two consecutive steps -- one per receive half -- into a CUDA
         graph on `stream` (partial_fn must launch on the current stream; with
         ``delivered``, partial_fn is a DecodeLaunch bound to `stream` and the
-        steps are ``step_delivered``).  The exchange kernels read their epoch
+        steps are ``step_delivered(partial_fn, owner)``).  The exchange kernels read their epoch
         from device memory, so the graph can be replayed any number of times
         with ``replay_pair``; every rank records and replays its pair in step
         with the others."""
@@ -268,7 +283,7 @@ class PeerExchange:
         with torch.cuda.graph(g, stream=stream):
             for _ in range(2):
                 if delivered:
-                    self.step_delivered(partial_fn)
+                    self.step_delivered(partial_fn, owner)
                 else:
                     self.step(partial_fn)
         self.steps -= 2   # they run when the graph is replayed

@@ -1,6 +1,7 @@
 """The sequence split's fused NVLink exchange + merge kernels
 (kvr_exchange_merge, and the delivered mode: kvr_decode_partial_exchange +
-kvr_exchange_merge_delivered).
+kvr_exchange_merge_delivered, or + kvr_exchange_merge_owned +
+kvr_exchange_gather_owned in owner mode).
 
 On one GPU: the kernel's time-limited wait for a peer that never signals
 runs out, sets the error flag and returns, and the next step completes; the
@@ -11,7 +12,7 @@ bit-identical to kvr_lse_merge, and its wait for ranks that skip a step
 runs out the same way.
 On two GPUs (skipped with fewer): the split against the single-GPU decode of
 the whole sequence, eagerly and as the replayed CUDA graph the benchmark
-times, at the benchmarked 28-layer 32K shape, in both modes.
+times, at the benchmarked 28-layer 32K shape, in every mode.
 """
 import ctypes
 import os
@@ -30,7 +31,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result, seq_len, layers, graph_steps, delivered):
+def _worker(rank, world, port, result, seq_len, layers, graph_steps, mode):
     import torch.distributed as dist
 
     import kv_reduce_b200 as kvr
@@ -63,7 +64,8 @@ def _worker(rank, world, port, result, seq_len, layers, graph_steps, delivered):
         ref = torch.cat([f.reshape(-1, wl.head_dim) for f in full])
         worst = 0.0
         for _ in range(4):   # both halves of the receive buffers, twice
-            out = (xchg.step_delivered(launch) if delivered else xchg.step(launch.partial)).float()
+            out = (xchg.step(launch.partial) if mode == "push"
+                   else xchg.step_delivered(launch, owner=mode == "owner")).float()
             torch.cuda.synchronize()
             worst = max(worst, float((out - ref).abs().max()))
         if graph_steps:
@@ -71,7 +73,8 @@ def _worker(rank, world, port, result, seq_len, layers, graph_steps, delivered):
             side = torch.cuda.Stream(device)
             launch_g = DecodeLaunch(geom, [_layer_ptrs(q, o, k, v) for q, o, k, v in zip(qs, dummy, ks, vs)],
                                     device, stream=side.cuda_stream)
-            graph = xchg.capture_pair(launch_g if delivered else launch_g.partial, side, delivered=delivered)
+            graph = xchg.capture_pair(launch_g.partial if mode == "push" else launch_g, side,
+                                      delivered=mode != "push", owner=mode == "owner")
             for _ in range(graph_steps):
                 xchg.replay_pair(graph)
                 torch.cuda.synchronize()
@@ -85,15 +88,15 @@ def _worker(rank, world, port, result, seq_len, layers, graph_steps, delivered):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("delivered", [False, True], ids=["push", "delivered"])
+@pytest.mark.parametrize("mode", ["push", "delivered", "owner"])
 @pytest.mark.parametrize("seq_len,layers,graph_steps", [(5000, 3, 0), (32768, 28, 3)])
-def test_two_gpu_sequence_split_fused_exchange(built_lib, seq_len, layers, graph_steps, delivered):
+def test_two_gpu_sequence_split_fused_exchange(built_lib, seq_len, layers, graph_steps, mode):
     import torch.multiprocessing as mp
 
     world = 2
     with mp.get_context("spawn").Manager() as manager:
         result = manager.dict()
-        mp.spawn(_worker, args=(world, _free_port(), result, seq_len, layers, graph_steps, delivered),
+        mp.spawn(_worker, args=(world, _free_port(), result, seq_len, layers, graph_steps, mode),
                  nprocs=world, join=True)
         for rank in range(world):
             worst, errors, scale = result[rank]
@@ -167,9 +170,12 @@ def test_exchange_wait_times_out_without_peer(built_lib):
     assert torch.allclose(out.float(), expect, rtol=2.0 ** -8, atol=1e-6)
 
 
+@pytest.mark.parametrize("owner", [False, True], ids=["to-all", "owner"])
 @pytest.mark.parametrize("world", [2, 3, 8])
-def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
-    """Delivered mode, `world` ranks emulated on one GPU.  Every receive
+def test_delivered_exchange_ranks_on_one_gpu(built_lib, world, owner):
+    """Delivered mode, `world` ranks emulated on one GPU, rows sent to every
+    rank or (owner) only to the rank that merges them, which then sends the
+    merged rows to every rank.  Every receive
     buffer and every rank's exchange state is local; the launches run in
     order on one stream (the decodes of ranks 0..world-1, then their
     merges), so every word a merge waits for was written by a decode that
@@ -177,8 +183,10 @@ def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
     area, as (value, epoch) words, is bit-identical to kvr_decode_partial
     over its shard, every word carries the step's epoch, every merge is
     bit-identical to kvr_lse_merge of all partials, and the result is the
-    single-GPU decode of the whole sequence within the bf16 bound.  Then
-    rank 0 alone takes a step and its bounded wait for the others runs out."""
+    single-GPU decode of the whole sequence within the bf16 bound.  In owner
+    mode each rank's area holds every source's words of the rows it owns,
+    and its final area every other owner's merged rows, tagged.  Then rank 0
+    alone takes a step and its bounded wait for the others runs out."""
     import kv_reduce_b200 as kvr
     from kv_reduce_b200 import _lib
     from kv_reduce_b200 import distributed as kd
@@ -219,7 +227,7 @@ def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
 
     slot = rows * (2 + D)
     data_floats = 2 * world * slot
-    bufs = [torch.zeros(data_floats + 64 + 2 * data_floats, dtype=torch.float32, device="cuda")
+    bufs = [torch.zeros(data_floats + 64 + 2 * data_floats + 2 * rows * D, dtype=torch.float32, device="cuda")
             for _ in range(world)]
     recv = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
     signal = recv + data_floats * 4
@@ -229,7 +237,13 @@ def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
     def xargs(r, timeout_ns=1_000_000_000):
         st = states[r].data_ptr()
         return _lib.ExchangeArgs(world, r, rows, D, recv.data_ptr(), signal.data_ptr(), st, st + 4, st + 8,
-                                 outs[r].data_ptr(), timeout_ns)
+                                 outs[r].data_ptr(), timeout_ns, 1 if owner else 0)
+
+    def merge(a):
+        if owner:
+            return (lib.kvr_exchange_merge_owned(ctypes.byref(a), stream),
+                    lib.kvr_exchange_gather_owned(ctypes.byref(a), stream))
+        return (lib.kvr_exchange_merge_delivered(ctypes.byref(a), stream),)
 
     args = [xargs(r) for r in range(world)]
     stream = torch.cuda.current_stream().cuda_stream
@@ -237,19 +251,31 @@ def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
         for r, ln in enumerate(launches):
             assert lib.kvr_decode_partial_exchange(ln.args, ln.token_begin, ln.token_end, ctypes.byref(args[r]),
                                                    stream) == _lib.KVR_OK
-        for r in range(world):
-            assert lib.kvr_exchange_merge_delivered(ctypes.byref(args[r]), stream) == _lib.KVR_OK
+        if owner:   # every owner merges before any rank gathers
+            for fn in (lib.kvr_exchange_merge_owned, lib.kvr_exchange_gather_owned):
+                for r in range(world):
+                    assert fn(ctypes.byref(args[r]), stream) == _lib.KVR_OK
+        else:
+            for r in range(world):
+                assert merge(args[r]) == (_lib.KVR_OK,)
         torch.cuda.synchronize()
         par = step & 1
         for r in range(world):
             assert states[r][2].item() == 0, "a wait timed out"
             assert states[r][0].item() == step and states[r][1].item() == 0
-            words = bufs[r].view(torch.int32)[data_floats + 64:].view(2, world, rows, 2 + D, 2)
+            words = bufs[r].view(torch.int32)[data_floats + 64:data_floats + 64 + 2 * data_floats]
+            words = words.view(2, world, rows, 2 + D, 2)
+            mine = torch.arange(rows, device="cuda") % world == r if owner else slice(None)
             for src in range(world):
-                w = words[par, src]
+                w = words[par, src][mine]
                 assert bool((w[..., 1] == step).all()), "a word does not carry the step's epoch"
-                assert torch.equal(w[:, :2, 0], parts[src][0].view(torch.int32)), (step, r, src)
-                assert torch.equal(w[:, 2:, 0], parts[src][1].view(torch.int32)), (step, r, src)
+                assert torch.equal(w[:, :2, 0], parts[src][0][mine].view(torch.int32)), (step, r, src)
+                assert torch.equal(w[:, 2:, 0], parts[src][1][mine].view(torch.int32)), (step, r, src)
+            if owner:
+                fin = bufs[r].view(torch.int32)[data_floats + 64 + 2 * data_floats:].view(2, rows, D // 2, 2)[par]
+                others = torch.arange(rows, device="cuda") % world != r
+                assert bool((fin[others][..., 1] == step).all())
+                assert torch.equal(fin[others][..., 0], merged[others].view(torch.int32))
             assert torch.equal(outs[r], merged), (step, r)
         err = (outs[0].float() - ref).abs().max().item()
         assert err <= 2e-3 + ref.abs().max().item() * 2.0 ** -8, err
@@ -262,7 +288,7 @@ def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
                                            stream) == _lib.KVR_OK
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    assert lib.kvr_exchange_merge_delivered(ctypes.byref(short), stream) == _lib.KVR_OK
+    assert all(st == _lib.KVR_OK for st in merge(short))
     torch.cuda.synchronize()
     waited = time.perf_counter() - t0
     assert states[0][2].item() == 1, "the time-out did not raise the error flag"
@@ -270,6 +296,6 @@ def test_delivered_exchange_ranks_on_one_gpu(built_lib, world):
     assert 0.04 <= waited < 5.0, waited
     # the exchange's rows must be the launch's layers x batch x q_heads
     bad = _lib.ExchangeArgs(world, 0, rows + 1, D, recv.data_ptr(), signal.data_ptr(), states[0].data_ptr(),
-                            states[0].data_ptr() + 4, states[0].data_ptr() + 8, outs[0].data_ptr(), 1)
+                            states[0].data_ptr() + 4, states[0].data_ptr() + 8, outs[0].data_ptr(), 1, int(owner))
     assert lib.kvr_decode_partial_exchange(launches[0].args, launches[0].token_begin, launches[0].token_end,
                                            ctypes.byref(bad), stream) == _lib.KVR_ERR_INVALID_ARGUMENT
