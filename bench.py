@@ -716,9 +716,11 @@ def run_ours(args, wl, world, rank, local):
         e2e = {"value": step_bytes * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes, "ms_per_step": e2e_ms,
                "path": "kv_reduce_b200.PackedDecoder.host_step (planned once) each step on the step's stacked "
-                       "pinned host queries: H2D copy of the queries and the decode of all layers, whose final "
-                       "merge writes the outputs into the pinned host buffer, replayed as one CUDA graph, then a "
-                       "wait for the outputs"}
+                       "pinned host queries: the decode of all layers reads them in place (one CTA per (layer, "
+                       "b, kv head) across PCIe, shared over distributed shared memory; an H2D copy when the "
+                       "plan has no clusters) and its final merge writes the outputs into the pinned host "
+                       "buffer, replayed as one CUDA graph, then a wait for the outputs",
+               "queries_in_place": bool(decoder._host and decoder._host.get("queries_in_place"))}
         e2e_l_ms = time_host(e2e_layers)
         e2e_layers_call = {"value": step_bytes * world / (e2e_l_ms * 1e-3) / 1e9, "unit": "GB/s",
                            "ms_per_step": e2e_l_ms,
